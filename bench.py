@@ -1,0 +1,371 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 MLA decode path; prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: absorbed-MLA decode, batch 64 per GPU,
+128 heads, kv_len 8192, latent 512 + rope 64, bf16, N(0,1) inputs.  A step is
+one decode call ``kernel(q, q_pe, kv, k_pe, out)`` (split-KV kernel + LSE
+combine).  With N GPUs (torchrun, one rank per GPU) every rank decodes its own
+64-sequence batch: the batch is partitioned across GPUs with no collective on
+the data path (weak scaling); the step time is the max over ranks.
+
+value       = device time per call (us), CUDA events over exactly K steps
+              bracketed by barrier + synchronize; inputs resident in HBM and
+              larger than L2 (604 MB per GPU), so no L2 flush is needed.
+roofline    = the split-KV kernel's algorithmic HBM bytes (b*s*576*2) per
+              launch / its mean CUDA-event duration in the same timed region,
+              against MEASURED_PEAKS.json's copy bandwidth.
+mla_roofline= north-star fraction for the whole call: max(bytes/HBM peak,
+              flops/bf16 peak) / measured us per call.
+e2e         = the same call through the public API with HOST buffers: pinned
+              host->device copies of q, q_pe, kv, k_pe and a device->host read
+              of out inside every timed step.
+cpu_baseline= the oracle's restatement of the reference torch path
+              (baseline_mla.py:167-191) on the host cores, on a bounded batch
+              sample, scaled to the full call.
+
+``--impl reference`` times only that reference CPU path (rank 0; other ranks
+exit without work) and prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MLA decode µs/call + % roofline (b64 h128 s8192 bf16) at 1/2/4/8 B200"
+UNIT = "us/call"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=64, help="sequences per GPU")
+    ap.add_argument("--heads", type=int, default=128)
+    ap.add_argument("--kv-ctx", type=int, default=8192)
+    ap.add_argument("--dtype", choices=["bf16", "fp16"], default="bf16")
+    ap.add_argument("--kernel", choices=["auto", "tc", "simt"], default="auto")
+    ap.add_argument("--num-split", type=int, default=0)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="budget of host-core time for the cpu_baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def workload_name(a):
+    return f"mla_decode b{a.batch}/gpu h{a.heads} s{a.kv_ctx} {a.dtype} (dim 512+64, kv_heads 1)"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "source": "measured"}
+    return dict(FALLBACK_PEAKS, source="fallback")
+
+
+def algorithmic(b, h, s):
+    return b * s * 576 * 2, 2.0 * b * h * s * (576 + 512)
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def mark(self, begin):
+        if begin:
+            self.t0 = time.time()
+        else:
+            self.t1 = time.time()
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 10:
+                    continue
+                try:
+                    ts = time.mktime(time.strptime(parts[1].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                    rows.append((ts, float(parts[2]), float(parts[3]), parts[6:10]))
+                except ValueError:
+                    continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        inside = [r for r in rows if self.t0 - 1.0 <= r[0] <= self.t1 + 1.0] or rows
+        reasons = sorted({self.NAMES[i] for r in inside for i, v in enumerate(r[3]) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": inside[0][2],
+                "reasons": reasons, "samples": len(inside)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference torch path restated by the oracle, on host cores
+# ---------------------------------------------------------------------------
+def cpu_time_per_call(a, budget_s, steps=None):
+    """Median seconds of ref_program_torch on a batch sample, scaled to the full call."""
+    import torch
+
+    from oracle.mla_oracle import make_inputs, ref_program_torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    probe = make_inputs(1, a.heads, a.kv_ctx, a.dtype, seed=0)
+    ref_program_torch(*probe)
+    t = time.perf_counter()
+    ref_program_torch(*probe)
+    t1 = max(time.perf_counter() - t, 1e-4)
+    reps = steps if steps is not None else 3
+    bs = int(max(1, min(a.batch, budget_s / (reps + 1) / t1)))
+    inp = make_inputs(bs, a.heads, a.kv_ctx, a.dtype, seed=0)
+    ref_program_torch(*inp)
+    times = []
+    for _ in range(reps):
+        t = time.perf_counter()
+        ref_program_torch(*inp)
+        times.append(time.perf_counter() - t)
+    return times, bs, torch.get_num_threads()
+
+
+def run_reference(a, rank):
+    if rank != 0:
+        return
+    warm = max(0, a.warmup)
+    times, bs, cores = cpu_time_per_call(a, a.cpu_seconds * 8, steps=a.steps + min(warm, 3))
+    times = times[min(warm, 3):] or times
+    us = statistics.median(times) * 1e6 * (a.batch / bs)
+    sample = (f"{bs} of {a.batch} sequences per step (same heads/kv_ctx/dtype), median of "
+              f"{len(times)} steps, scaled x{a.batch / bs:g} to the full call")
+    line = {"impl": "reference", "metric": METRIC, "value": round(us, 3), "unit": UNIT,
+            "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": round(us / 1000, 3), "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": a.dtype, "data": "synthetic N(0,1), seeded",
+            "config": {"workload": workload_name(a), "batch_per_gpu": a.batch, "heads": a.heads,
+                       "kv_ctx": a.kv_ctx, "parallelism": "reference CPU path, host cores"},
+            "cpu_baseline": {"value": round(us, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(us, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def traffic_from_profiles(a):
+    """Per-launch DRAM bytes of the split-KV kernel from a committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        d = json.load(f)
+    ent = d.get(f"b{a.batch}_h{a.heads}_s{a.kv_ctx}_{a.dtype}_{a.kernel}") or \
+        d.get(f"b{a.batch}_h{a.heads}_s{a.kv_ctx}_{a.dtype}")
+    return None if ent is None else ent.get("dram_bytes_per_launch")
+
+
+def run_ours(a, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from mlc_decode_b200 import MlaDecodeKernel
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    b, h, s = a.batch, a.heads, a.kv_ctx
+    tdt = torch.bfloat16 if a.dtype == "bf16" else torch.float16
+    cfg = {"kernel": a.kernel}
+    if a.num_split:
+        cfg["num_split"] = a.num_split
+    kern = MlaDecodeKernel(b, h, 1, s, cfg=cfg)
+
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    q = torch.randn(b, h, 512, device=dev, generator=g).to(tdt)
+    q_pe = torch.randn(b, h, 64, device=dev, generator=g).to(tdt)
+    kv = torch.randn(b, s, 1, 512, device=dev, generator=g).to(tdt)
+    k_pe = torch.randn(b, s, 1, 64, device=dev, generator=g).to(tdt)
+    out = torch.empty_like(q)
+    launches = kern.launches_per_call(tdt)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(max(3, a.warmup)):
+        kern(q, q_pe, kv, k_pe, out)
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    K = a.steps
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.mark(True)
+    start.record()
+    for i in range(K):
+        ev_a[i].record()
+        kern.splitkv(q, q_pe, kv, k_pe, out)
+        ev_b[i].record()
+        kern.combine_ws(out)
+    end.record()
+    torch.cuda.synchronize()
+    clocks.mark(False)
+    barrier()
+    clk = clocks.stop()
+    total_ms = start.elapsed_time(end)
+    dec_ms = [ev_a[i].elapsed_time(ev_b[i]) for i in range(K)]
+    t = torch.tensor([total_ms, statistics.mean(dec_ms)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, dec_mean_ms = float(t[0]), float(t[1])
+    us_call = total_ms * 1000.0 / K
+    dec_us = dec_mean_ms * 1000.0
+
+    # ---- e2e through the public API with host buffers ------------------------
+    hq, hqp, hkv, hkp = (x.cpu().pin_memory() for x in (q, q_pe, kv, k_pe))
+    hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    dq, dqp, dkv, dkp = (torch.empty_like(x) for x in (q, q_pe, kv, k_pe))
+    E = max(3, min(a.e2e_steps, K))
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dqp.copy_(hqp, non_blocking=True)
+        dkv.copy_(hkv, non_blocking=True)
+        dkp.copy_(hkp, non_blocking=True)
+        kern(dq, dqp, dkv, dkp, out)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(E):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_us = float(te[0]) * 1000.0 / E
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hqp, hkv, hkp))
+    d2h = hout.numel() * hout.element_size()
+    del hq, hqp, hkv, hkp, dq, dqp, dkv, dkp
+
+    if rank != 0:
+        return
+    peaks = load_peaks()
+    bytes_alg, flops_alg = algorithmic(b, h, s)
+    achieved = bytes_alg / (dec_us * 1e-6) / 1e9
+    t_roof_us = max(bytes_alg / (peaks["hbm_gbs"] * 1e9), flops_alg / (peaks["bf16_tflops"] * 1e12)) * 1e6
+    line = {
+        "metric": METRIC, "value": round(us_call, 3), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": a.warmup, "ms_per_step": round(us_call / 1000.0, 5), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": a.dtype,
+        "data": "synthetic N(0,1), seeded, generated on device",
+        "config": {"workload": workload_name(a), "batch_per_gpu": b, "global_batch": b * world,
+                   "heads": h, "kv_ctx": s, "kernel": a.kernel, "num_split": a.num_split or "auto",
+                   "parallelism": f"batch split over {world} GPU(s), no collective",
+                   "l2": "inputs (KV+K_pe %.0f MB per GPU) larger than the 126 MB L2; no flush"
+                         % (bytes_alg / 1e6)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "traffic": traffic_from_profiles(a), "kernel": "split-KV decode kernel",
+                     "kernel_us": round(dec_us, 3), "peak_source": peaks["source"]},
+        "mla_roofline": {"t_roof_us": round(t_roof_us, 3),
+                         "frac": round(t_roof_us / us_call, 4),
+                         "hbm_bytes": bytes_alg, "flops": flops_alg,
+                         "peaks": {"hbm_gbs": peaks["hbm_gbs"], "bf16_tflops": peaks["bf16_tflops"],
+                                   "source": peaks["source"]}},
+        "e2e": {"value": round(e2e_us, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": E},
+        "gpu_launches": K * launches,
+        "clocks": clk,
+    }
+    if world == 1 and not a.no_cpu_baseline:
+        times, bs, cores = cpu_time_per_call(a, a.cpu_seconds)
+        cpu_us = statistics.median(times) * 1e6 * (b / bs)
+        line["cpu_baseline"] = {"value": round(cpu_us, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": f"{bs} of {b} sequences, median of {len(times)} runs, "
+                                          f"scaled x{b / bs:g} to the full call"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference(a, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(a, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

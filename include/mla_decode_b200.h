@@ -1,0 +1,143 @@
+/*
+ * mla_decode_b200.h -- C ABI of the B200 (sm_100a) absorbed-MLA decode path.
+ *
+ * Layout of every tensor argument (row-major, contiguous, device pointers):
+ *   q      [batch, heads, 512]        fp16 or bf16 (dtype)
+ *   q_pe   [batch, heads, 64]         same dtype
+ *   kv     [batch, seqlen_kv, 1, 512] same dtype  (latent: keys AND values)
+ *   k_pe   [batch, seqlen_kv, 1, 64]  same dtype  (rope part of the keys)
+ *   out    [batch, heads, 512]        same dtype, caller-allocated, written
+ *   lse    [batch, heads]             float32 natural-log log-sum-exp, optional
+ *
+ * out[b,h,:] = softmax_s(([q|q_pe] . [kv|k_pe]^T) / sqrt(576)) . kv.
+ *
+ * Every entry point returns MLA_OK (0) or an error code; nothing throws across
+ * the ABI, and mla_last_error() gives the calling thread's last message.
+ * Launch entry points enqueue on `stream` (a cudaStream_t, NULL = legacy
+ * default stream) and never synchronise the host.  Calls on distinct streams
+ * from distinct threads are safe; per-device kernel attributes are set once.
+ */
+#ifndef MLA_DECODE_B200_H_
+#define MLA_DECODE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MLA_ABI_VERSION 1
+
+enum MlaDtype { MLA_DTYPE_F16 = 0, MLA_DTYPE_BF16 = 1 };
+
+enum MlaStatus {
+  MLA_OK = 0,
+  MLA_ERR_ARG = 1,          /* bad shape, pointer, alignment or config */
+  MLA_ERR_WORKSPACE = 2,    /* workspace missing or too small */
+  MLA_ERR_UNSUPPORTED = 3,  /* shape/config outside what the kernels cover */
+  MLA_ERR_CUDA = 4,         /* a CUDA runtime/driver call failed */
+  MLA_ERR_DEVICE = 5        /* a kernel reported a failure through its status word */
+};
+
+/* Which decode kernel runs. */
+enum MlaKernelKind {
+  MLA_KERNEL_AUTO = 0,   /* tensor-core kernel where it covers the shape, else SIMT */
+  MLA_KERNEL_SIMT = 1,   /* CUDA-core split-KV kernel (any heads, any seqlen) */
+  MLA_KERNEL_TC = 2      /* tcgen05/TMA/TMEM split-KV kernel (sm_100a) */
+};
+
+/*
+ * Tuning knobs.  Same names and meaning as the reference's config dict
+ * (mla_decode.py:588-598, 720-729): block_N KV rows per tile, block_H heads
+ * per CTA, num_split requested KV splits per sequence, spread selects the
+ * whole-wave split family of _split_plan (mla_decode.py:9-30), num_stages the
+ * depth of the shared-memory pipeline.  combine_groups is accepted and
+ * ignored (the combine kernel is single pass).  softmax_scale is the factory
+ * argument of the same name (mla_decode.py:38).  Zero fields mean "choose".
+ */
+typedef struct MlaCfg {
+  int32_t block_N;
+  int32_t block_H;
+  int32_t num_split;
+  int32_t spread;
+  int32_t num_stages;
+  int32_t combine_groups;
+  int32_t kernel;         /* enum MlaKernelKind */
+  float softmax_scale;    /* multiplies the raw scores; 0 = 1/sqrt(576) */
+} MlaCfg;
+
+/* Version of this ABI (MLA_ABI_VERSION). */
+int32_t mla_abi_version(void);
+
+/* Thread-local text of the last error returned on this thread ("" if none). */
+const char* mla_last_error(void);
+
+/*
+ * _split_plan (mla_decode.py:9-30): nb = ceil(seqlen_kv / block_n) KV tiles
+ * go to ns splits.  Writes {ns, blocks_per_split, extra} to out3.
+ */
+int32_t mla_split_plan(int32_t seqlen_kv, int32_t num_split, int32_t block_n,
+                       int32_t spread, int32_t* out3);
+
+/*
+ * Bytes of device scratch mla_decode_fwd needs for this shape and config
+ * (partial O and partial LSE per split, float32).  Replaces the per-call
+ * T.alloc_global of glse / output_partial (mla_decode.py:73-76).
+ * Returns 0 on a bad argument (see mla_last_error).
+ */
+size_t mla_workspace_bytes(int32_t batch, int32_t heads, int32_t seqlen_kv,
+                           int32_t dtype, const MlaCfg* cfg);
+
+/*
+ * One decode call: the split-KV main kernel then the LSE combine kernel,
+ * enqueued on `stream`.  Replaces the TileLang prim_func `main`
+ * (mla_decode.py:65-259) that kernel(q, q_pe, kv, k_pe, out) launches, and the
+ * handmade launcher mla_launch(Q, Qpe, KV, Kpe, glse, partial, out, ns)
+ * (handmade/mla_handmade.py:32-53).  `workspace` must hold
+ * mla_workspace_bytes(...) bytes (256-byte aligned).  lse may be NULL.
+ * cfg may be NULL (all fields "choose").
+ */
+int32_t mla_decode_fwd(const void* q, const void* q_pe, const void* kv,
+                       const void* k_pe, void* out, float* lse,
+                       void* workspace, size_t workspace_bytes,
+                       int32_t batch, int32_t heads, int32_t seqlen_kv,
+                       int32_t dtype, const MlaCfg* cfg, void* stream);
+
+/*
+ * mla_decode_fwd in its two launches, for callers that interleave their own
+ * work or events between them (same arguments and checks as mla_decode_fwd):
+ * mla_decode_splitkv enqueues the split-KV main kernel (mla_decode.py:78-192),
+ * which leaves per-split partials in `workspace` (or, for a single-split plan,
+ * writes out/lse directly); mla_decode_combine_ws then enqueues the combine
+ * kernel (mla_decode.py:194-246) over that workspace, and is a no-op for a
+ * single-split plan.  Both must see the same shape, dtype and cfg.
+ */
+int32_t mla_decode_splitkv(const void* q, const void* q_pe, const void* kv,
+                           const void* k_pe, void* out, float* lse,
+                           void* workspace, size_t workspace_bytes,
+                           int32_t batch, int32_t heads, int32_t seqlen_kv,
+                           int32_t dtype, const MlaCfg* cfg, void* stream);
+int32_t mla_decode_combine_ws(void* out, float* lse, const void* workspace,
+                              size_t workspace_bytes, int32_t batch,
+                              int32_t heads, int32_t seqlen_kv, int32_t dtype,
+                              const MlaCfg* cfg, void* stream);
+
+/*
+ * LSE combine of num_split normalised partial results (the second kernel of
+ * mla_decode.py:194-246, natural-log units):
+ *   part_lse [num_split, batch, heads]       float32 (-inf = empty split)
+ *   part_o   [num_split, batch, heads, 512]  float32
+ * out[b,h,:] = sum_k exp(lse_k - LSE) * o_k with LSE = logsumexp_k(lse_k);
+ * lse (optional) receives LSE.  Also merges per-GPU results of a
+ * sequence-split decode after they are gathered into one buffer.
+ */
+int32_t mla_combine(const float* part_lse, const float* part_o,
+                    int32_t num_split, int32_t batch, int32_t heads,
+                    void* out, float* lse, int32_t dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLA_DECODE_B200_H_ */

@@ -1,0 +1,156 @@
+"""ctypes binding of ``libmla_decode_b200.so`` (C ABI in include/mla_decode_b200.h).
+
+The library is loaded from this package directory.  There is no fallback:
+if it is missing or fails to load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from . import build as _build
+
+MLA_DTYPE_F16 = 0
+MLA_DTYPE_BF16 = 1
+
+MLA_KERNEL_AUTO = 0
+MLA_KERNEL_SIMT = 1
+MLA_KERNEL_TC = 2
+
+STATUS_NAMES = {0: "MLA_OK", 1: "MLA_ERR_ARG", 2: "MLA_ERR_WORKSPACE", 3: "MLA_ERR_UNSUPPORTED",
+                4: "MLA_ERR_CUDA", 5: "MLA_ERR_DEVICE"}
+
+EXPORTED_SYMBOLS = ("mla_abi_version", "mla_last_error", "mla_split_plan",
+                    "mla_workspace_bytes", "mla_decode_fwd", "mla_decode_splitkv",
+                    "mla_decode_combine_ws", "mla_combine")
+
+
+class MlaCfg(ctypes.Structure):
+    """struct MlaCfg (include/mla_decode_b200.h)."""
+
+    _fields_ = [("block_N", ctypes.c_int32), ("block_H", ctypes.c_int32),
+                ("num_split", ctypes.c_int32), ("spread", ctypes.c_int32),
+                ("num_stages", ctypes.c_int32), ("combine_groups", ctypes.c_int32),
+                ("kernel", ctypes.c_int32), ("softmax_scale", ctypes.c_float)]
+
+
+class MlaError(RuntimeError):
+    """A non-zero status returned through the C ABI."""
+
+    def __init__(self, status, message):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib_path() -> str:
+    return _build.LIB_PATH
+
+
+def load(build_if_missing: bool = True):
+    """Load (building first if allowed and needed) and return the CDLL."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = lib_path()
+        if build_if_missing and not _build.up_to_date():
+            try:
+                _build.build()
+            except RuntimeError:
+                if not os.path.exists(path):
+                    raise
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is missing: run `python -m mlc_decode_b200.build`")
+        lib = ctypes.CDLL(path)
+        vp, i32, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t
+        lib.mla_abi_version.argtypes = []
+        lib.mla_abi_version.restype = i32
+        lib.mla_last_error.argtypes = []
+        lib.mla_last_error.restype = ctypes.c_char_p
+        lib.mla_split_plan.argtypes = [i32, i32, i32, i32, ctypes.POINTER(i32)]
+        lib.mla_split_plan.restype = i32
+        lib.mla_workspace_bytes.argtypes = [i32, i32, i32, i32, ctypes.POINTER(MlaCfg)]
+        lib.mla_workspace_bytes.restype = sz
+        lib.mla_decode_fwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, sz, i32, i32, i32, i32,
+                                       ctypes.POINTER(MlaCfg), vp]
+        lib.mla_decode_fwd.restype = i32
+        lib.mla_decode_splitkv.argtypes = lib.mla_decode_fwd.argtypes
+        lib.mla_decode_splitkv.restype = i32
+        lib.mla_decode_combine_ws.argtypes = [vp, vp, vp, sz, i32, i32, i32, i32,
+                                              ctypes.POINTER(MlaCfg), vp]
+        lib.mla_decode_combine_ws.restype = i32
+        lib.mla_combine.argtypes = [vp, vp, i32, i32, i32, vp, vp, i32, vp]
+        lib.mla_combine.restype = i32
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    return load().mla_last_error().decode(errors="replace")
+
+
+def check(status: int):
+    if status != 0:
+        raise MlaError(status, last_error())
+
+
+def make_cfg(cfg: dict | None = None, kernel: int | None = None) -> MlaCfg:
+    """Map a reference-style config dict (mla_decode.py:588-598) to MlaCfg."""
+    cfg = cfg or {}
+    c = MlaCfg()
+    c.block_N = int(cfg.get("block_N", 0) or 0)
+    c.block_H = int(cfg.get("block_H", 0) or 0)
+    c.num_split = int(cfg.get("num_split", 0) or 0)
+    c.spread = int(bool(cfg.get("spread", False)))
+    c.num_stages = int(cfg.get("num_stages", 0) or 0)
+    c.combine_groups = int(cfg.get("combine_groups", 1) or 1)
+    k = cfg.get("kernel", kernel)
+    if isinstance(k, str):
+        k = {"auto": MLA_KERNEL_AUTO, "simt": MLA_KERNEL_SIMT, "tc": MLA_KERNEL_TC}[k]
+    c.kernel = int(k or 0)
+    c.softmax_scale = float(cfg.get("softmax_scale", 0.0) or 0.0)
+    return c
+
+
+def split_plan(seqlen_kv: int, num_split: int, block_n: int, spread: bool = False):
+    out = (ctypes.c_int32 * 3)()
+    check(load().mla_split_plan(int(seqlen_kv), int(num_split), int(block_n), int(bool(spread)), out))
+    return int(out[0]), int(out[1]), int(out[2])
+
+
+def workspace_bytes(batch, heads, seqlen_kv, dtype, cfg: MlaCfg) -> int:
+    n = load().mla_workspace_bytes(int(batch), int(heads), int(seqlen_kv), int(dtype), ctypes.byref(cfg))
+    if n == 0:
+        msg = last_error()
+        if msg:
+            raise MlaError(1, msg)
+    return int(n)
+
+
+def decode_fwd(q, q_pe, kv, k_pe, out, lse, ws, ws_bytes, batch, heads, seqlen_kv, dtype,
+               cfg: MlaCfg, stream) -> None:
+    """Raw pointers in, status checked.  Pointers are ints (device addresses)."""
+    check(load().mla_decode_fwd(q, q_pe, kv, k_pe, out, lse, ws, ws_bytes, int(batch), int(heads),
+                                int(seqlen_kv), int(dtype), ctypes.byref(cfg), stream))
+
+
+def decode_splitkv(q, q_pe, kv, k_pe, out, lse, ws, ws_bytes, batch, heads, seqlen_kv, dtype,
+                   cfg: MlaCfg, stream) -> None:
+    check(load().mla_decode_splitkv(q, q_pe, kv, k_pe, out, lse, ws, ws_bytes, int(batch), int(heads),
+                                    int(seqlen_kv), int(dtype), ctypes.byref(cfg), stream))
+
+
+def decode_combine_ws(out, lse, ws, ws_bytes, batch, heads, seqlen_kv, dtype, cfg: MlaCfg,
+                      stream) -> None:
+    check(load().mla_decode_combine_ws(out, lse, ws, ws_bytes, int(batch), int(heads), int(seqlen_kv),
+                                       int(dtype), ctypes.byref(cfg), stream))
+
+
+def combine(part_lse, part_o, num_split, batch, heads, out, lse, dtype, stream) -> None:
+    check(load().mla_combine(part_lse, part_o, int(num_split), int(batch), int(heads), out, lse,
+                             int(dtype), stream))

@@ -1,0 +1,297 @@
+// extern "C" entry points of libmla_decode_b200.so (declared in
+// include/mla_decode_b200.h).  Argument checking, kernel choice, split planning
+// and workspace carving live here; the kernels live in their own files.
+#include <stdarg.h>
+#include <stdio.h>
+#include <math.h>
+#include <string.h>
+
+#include <string>
+
+#include "mla_common.cuh"
+#include "mla_sm100.cuh"
+
+namespace mla {
+
+namespace {
+thread_local std::string g_last_error;
+constexpr int kSmCount = 148;
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+}
+
+namespace {
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Resolved launch: which kernel, and the split plan it uses.
+struct Resolved {
+  int kernel;
+  SplitPlan plan;
+  int tc_variant;  // sm100 kernel variant (see mla_sm100.cuh)
+};
+
+int check_shape(int batch, int heads, int seqlen_kv, int dtype) {
+  if (batch < 1 || heads < 1 || seqlen_kv < 1) {
+    set_error("mla: batch, heads and seqlen_kv must be >= 1 (got %d, %d, %d)", batch, heads, seqlen_kv);
+    return MLA_ERR_ARG;
+  }
+  if (dtype != MLA_DTYPE_F16 && dtype != MLA_DTYPE_BF16) {
+    set_error("mla: dtype must be 0 (fp16) or 1 (bf16), got %d", dtype);
+    return MLA_ERR_ARG;
+  }
+  if ((long long)batch * heads > (1ll << 30) || (long long)batch * seqlen_kv > (1ll << 40)) {
+    set_error("mla: shape too large");
+    return MLA_ERR_ARG;
+  }
+  return MLA_OK;
+}
+
+int resolve(int batch, int heads, int seqlen_kv, const MlaCfg* cfg, Resolved* r) {
+  MlaCfg c{};
+  if (cfg != nullptr) c = *cfg;
+  int kind = c.kernel;
+  if (kind != MLA_KERNEL_AUTO && kind != MLA_KERNEL_SIMT && kind != MLA_KERNEL_TC) {
+    set_error("mla: unknown kernel kind %d", kind);
+    return MLA_ERR_ARG;
+  }
+  const bool tc_ok = sm100_supports(heads, seqlen_kv);
+  if (kind == MLA_KERNEL_TC && !tc_ok) {
+    set_error("mla: the tensor-core kernel does not cover heads=%d seqlen_kv=%d", heads, seqlen_kv);
+    return MLA_ERR_UNSUPPORTED;
+  }
+  if (kind == MLA_KERNEL_AUTO) kind = tc_ok ? MLA_KERNEL_TC : MLA_KERNEL_SIMT;
+  r->kernel = kind;
+  if (c.num_split < 0 || c.block_N < 0) {
+    set_error("mla: num_split and block_N must be >= 0");
+    return MLA_ERR_ARG;
+  }
+  if (kind == MLA_KERNEL_SIMT) {
+    int bn = c.block_N > 0 ? c.block_N : simt_block_n();
+    if (bn % simt_block_n() != 0) {
+      set_error("mla: SIMT kernel needs block_N a multiple of %d (got %d)", simt_block_n(), bn);
+      return MLA_ERR_ARG;
+    }
+    int ns = c.num_split;
+    bool spread = c.spread != 0;
+    if (ns == 0) {
+      // enough CTAs for two resident waves over all SMs
+      const long long units = (long long)batch * ((heads + 15) / 16);
+      const long long target = (long long)kSmCount * simt_ctas_per_sm() * 2;
+      ns = (int)((target + units - 1) / units);
+      spread = true;
+    }
+    r->plan = split_plan(seqlen_kv, ns, bn, spread);
+    r->tc_variant = 0;
+  } else {
+    r->plan = sm100_plan(batch, heads, seqlen_kv, c, &r->tc_variant);
+  }
+  if (r->plan.ns > 8192) {
+    set_error("mla: num_split %d exceeds 8192", r->plan.ns);
+    return MLA_ERR_ARG;
+  }
+  return MLA_OK;
+}
+
+size_t workspace_for(int batch, int heads, const Resolved& r) {
+  if (r.kernel == MLA_KERNEL_SIMT && r.plan.ns == 1) return 0;
+  const size_t rows = (size_t)r.plan.ns * batch * heads;
+  return align_up(rows * sizeof(float), 256) + rows * kDim * sizeof(float);
+}
+
+}  // namespace
+}  // namespace mla
+
+using namespace mla;
+
+extern "C" {
+
+int32_t mla_abi_version(void) { return MLA_ABI_VERSION; }
+
+const char* mla_last_error(void) { return g_last_error.c_str(); }
+
+int32_t mla_split_plan(int32_t seqlen_kv, int32_t num_split, int32_t block_n, int32_t spread,
+                       int32_t* out3) {
+  if (out3 == nullptr || seqlen_kv < 0 || block_n < 1) {
+    set_error("mla_split_plan: bad argument");
+    return MLA_ERR_ARG;
+  }
+  const SplitPlan p = split_plan(seqlen_kv, num_split, block_n, spread != 0);
+  out3[0] = p.ns;
+  out3[1] = p.bpc;
+  out3[2] = p.extra;
+  return MLA_OK;
+}
+
+size_t mla_workspace_bytes(int32_t batch, int32_t heads, int32_t seqlen_kv, int32_t dtype,
+                           const MlaCfg* cfg) {
+  if (check_shape(batch, heads, seqlen_kv, dtype) != MLA_OK) return 0;
+  Resolved r{};
+  if (resolve(batch, heads, seqlen_kv, cfg, &r) != MLA_OK) return 0;
+  return workspace_for(batch, heads, r);
+}
+
+}  // extern "C"
+
+namespace mla {
+namespace {
+
+// Validate one decode call and fill the launch arguments.  `need_inputs`
+// is false for the combine-only entry point (q/q_pe/kv/k_pe unused).
+int prepare(const char* fn, const void* q, const void* q_pe, const void* kv, const void* k_pe,
+            void* out, float* lse, const void* workspace, size_t workspace_bytes, int batch,
+            int heads, int seqlen_kv, int dtype, const MlaCfg* cfg, void* stream, bool need_inputs,
+            DecodeArgs* a, Resolved* r, size_t* need) {
+  int rc = check_shape(batch, heads, seqlen_kv, dtype);
+  if (rc != MLA_OK) return rc;
+  if ((need_inputs && (!q || !q_pe || !kv || !k_pe)) || !out) {
+    set_error("%s: null tensor pointer", fn);
+    return MLA_ERR_ARG;
+  }
+  if ((need_inputs && (!aligned16(q) || !aligned16(q_pe) || !aligned16(kv) || !aligned16(k_pe))) ||
+      !aligned16(out)) {
+    set_error("%s: tensor pointers must be 16-byte aligned", fn);
+    return MLA_ERR_ARG;
+  }
+  rc = resolve(batch, heads, seqlen_kv, cfg, r);
+  if (rc != MLA_OK) return rc;
+  *need = workspace_for(batch, heads, *r);
+  if (*need > 0 && (workspace == nullptr || workspace_bytes < *need ||
+                    (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)) {
+    set_error("%s: workspace needs %zu bytes, 256-byte aligned (got %zu at %p)", fn, *need,
+              workspace_bytes, workspace);
+    return MLA_ERR_WORKSPACE;
+  }
+  *a = DecodeArgs{};
+  a->q = q;
+  a->q_pe = q_pe;
+  a->kv = kv;
+  a->k_pe = k_pe;
+  a->out = out;
+  a->lse = lse;
+  a->batch = batch;
+  a->heads = heads;
+  a->seqlen_kv = seqlen_kv;
+  a->dtype = dtype;
+  a->softmax_scale = (cfg != nullptr && cfg->softmax_scale != 0.f) ? cfg->softmax_scale
+                                                                   : 1.0f / sqrtf((float)kQkDim);
+  if (!(a->softmax_scale > 0.f) || !isfinite(a->softmax_scale)) {
+    set_error("%s: softmax_scale must be finite and > 0", fn);
+    return MLA_ERR_ARG;
+  }
+  a->plan = r->plan;
+  a->stream = static_cast<cudaStream_t>(stream);
+  if (*need > 0) {
+    const size_t rows = (size_t)r->plan.ns * batch * heads;
+    a->part_lse = static_cast<float*>(const_cast<void*>(workspace));
+    a->part_o = reinterpret_cast<float*>(static_cast<char*>(const_cast<void*>(workspace)) +
+                                         align_up(rows * sizeof(float), 256));
+  }
+  return MLA_OK;
+}
+
+int run_splitkv(const char* fn, const DecodeArgs& a, const Resolved& r) {
+  const cudaError_t err =
+      r.kernel == MLA_KERNEL_SIMT ? launch_simt_decode(a) : launch_sm100_decode(a, r.tc_variant);
+  if (err != cudaSuccess) {
+    set_error("%s: decode launch failed: %s", fn, cudaGetErrorString(err));
+    return MLA_ERR_CUDA;
+  }
+  return MLA_OK;
+}
+
+int run_combine_ws(const char* fn, const DecodeArgs& a, const Resolved& r, size_t need) {
+  if (need == 0) return MLA_OK;   // single-split plan: the decode kernel wrote out/lse
+  const cudaError_t err = launch_combine(a.part_lse, a.part_o, r.plan.ns, a.batch, a.heads, a.out,
+                                         a.lse, a.dtype, a.stream);
+  if (err != cudaSuccess) {
+    set_error("%s: combine launch failed: %s", fn, cudaGetErrorString(err));
+    return MLA_ERR_CUDA;
+  }
+  return MLA_OK;
+}
+
+}  // namespace
+}  // namespace mla
+
+extern "C" {
+
+int32_t mla_decode_fwd(const void* q, const void* q_pe, const void* kv, const void* k_pe,
+                       void* out, float* lse, void* workspace, size_t workspace_bytes,
+                       int32_t batch, int32_t heads, int32_t seqlen_kv, int32_t dtype,
+                       const MlaCfg* cfg, void* stream) {
+  DecodeArgs a;
+  Resolved r;
+  size_t need = 0;
+  int rc = prepare("mla_decode_fwd", q, q_pe, kv, k_pe, out, lse, workspace, workspace_bytes, batch,
+                   heads, seqlen_kv, dtype, cfg, stream, true, &a, &r, &need);
+  if (rc != MLA_OK) return rc;
+  rc = run_splitkv("mla_decode_fwd", a, r);
+  if (rc != MLA_OK) return rc;
+  return run_combine_ws("mla_decode_fwd", a, r, need);
+}
+
+int32_t mla_decode_splitkv(const void* q, const void* q_pe, const void* kv, const void* k_pe,
+                           void* out, float* lse, void* workspace, size_t workspace_bytes,
+                           int32_t batch, int32_t heads, int32_t seqlen_kv, int32_t dtype,
+                           const MlaCfg* cfg, void* stream) {
+  DecodeArgs a;
+  Resolved r;
+  size_t need = 0;
+  const int rc = prepare("mla_decode_splitkv", q, q_pe, kv, k_pe, out, lse, workspace,
+                         workspace_bytes, batch, heads, seqlen_kv, dtype, cfg, stream, true, &a, &r,
+                         &need);
+  if (rc != MLA_OK) return rc;
+  return run_splitkv("mla_decode_splitkv", a, r);
+}
+
+int32_t mla_decode_combine_ws(void* out, float* lse, const void* workspace, size_t workspace_bytes,
+                              int32_t batch, int32_t heads, int32_t seqlen_kv, int32_t dtype,
+                              const MlaCfg* cfg, void* stream) {
+  DecodeArgs a;
+  Resolved r;
+  size_t need = 0;
+  const int rc = prepare("mla_decode_combine_ws", nullptr, nullptr, nullptr, nullptr, out, lse,
+                         workspace, workspace_bytes, batch, heads, seqlen_kv, dtype, cfg, stream,
+                         false, &a, &r, &need);
+  if (rc != MLA_OK) return rc;
+  return run_combine_ws("mla_decode_combine_ws", a, r, need);
+}
+
+int32_t mla_combine(const float* part_lse, const float* part_o, int32_t num_split, int32_t batch,
+                    int32_t heads, void* out, float* lse, int32_t dtype, void* stream) {
+  if (!part_lse || !part_o || !out) {
+    set_error("mla_combine: null pointer");
+    return MLA_ERR_ARG;
+  }
+  if (num_split < 1 || num_split > 8192 || batch < 1 || heads < 1) {
+    set_error("mla_combine: bad num_split/batch/heads (%d, %d, %d)", num_split, batch, heads);
+    return MLA_ERR_ARG;
+  }
+  if (dtype != MLA_DTYPE_F16 && dtype != MLA_DTYPE_BF16) {
+    set_error("mla_combine: dtype must be 0 or 1");
+    return MLA_ERR_ARG;
+  }
+  if (!aligned16(part_o) || !aligned16(out)) {
+    set_error("mla_combine: part_o and out must be 16-byte aligned");
+    return MLA_ERR_ARG;
+  }
+  const cudaError_t err = launch_combine(part_lse, part_o, num_split, batch, heads, out, lse, dtype,
+                                         static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) {
+    set_error("mla_combine: launch failed: %s", cudaGetErrorString(err));
+    return MLA_ERR_CUDA;
+  }
+  return MLA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,127 @@
+// Shared definitions of the sm_100a MLA decode library: constants, element
+// conversions, the KV split planner and the launcher prototypes that the C ABI
+// (mla_capi.cu) dispatches to.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/mla_decode_b200.h"
+
+namespace mla {
+
+constexpr int kDim = 512;      // latent width (keys and values)
+constexpr int kPeDim = 64;     // rope width (keys only)
+constexpr int kQkDim = kDim + kPeDim;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// ---------------------------------------------------------------------------
+// element conversions
+// ---------------------------------------------------------------------------
+template <typename T> struct Elt;
+template <> struct Elt<__half> {
+  static __device__ __forceinline__ float2 to2(uint32_t w) {
+    __half2 h = *reinterpret_cast<__half2*>(&w);
+    return __half22float2(h);
+  }
+  static __device__ __forceinline__ float to1(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ __half from(float x) { return __float2half_rn(x); }
+  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+template <> struct Elt<__nv_bfloat16> {
+  static __device__ __forceinline__ float2 to2(uint32_t w) {
+    __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&w);
+    return __bfloat1622float2(h);
+  }
+  static __device__ __forceinline__ float to1(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from(float x) { return __float2bfloat16_rn(x); }
+  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+// ---------------------------------------------------------------------------
+// split planner: _split_plan (mla_decode.py:9-30)
+// ---------------------------------------------------------------------------
+struct SplitPlan {
+  int ns;            // number of splits actually used
+  int bpc;           // KV tiles per split
+  int extra;         // the first `extra` splits take one more tile
+  int block_n;       // KV rows per tile
+};
+
+inline SplitPlan split_plan(int seqlen_kv, int num_split, int block_n, bool spread) {
+  SplitPlan p{};
+  p.block_n = block_n;
+  const int nb = (seqlen_kv + block_n - 1) / block_n;
+  if (num_split < 1) num_split = 1;
+  if (!spread) {
+    const int chunk = (seqlen_kv + num_split - 1) / num_split;
+    p.bpc = (chunk + block_n - 1) / block_n;
+    if (p.bpc < 1) p.bpc = 1;
+    p.ns = (nb + p.bpc - 1) / p.bpc;
+    if (p.ns < 1) p.ns = 1;
+    p.extra = 0;
+  } else {
+    p.ns = num_split < nb ? num_split : nb;
+    if (p.ns < 1) p.ns = 1;
+    p.bpc = nb / p.ns;
+    p.extra = nb % p.ns;
+  }
+  return p;
+}
+
+// Token range [t0, t1) of split z under plan p (mla_decode.py:113-120; rows past
+// seqlen_kv are masked in the reference, i.e. the range is clipped).
+__host__ __device__ __forceinline__ void split_range(int z, int bpc, int extra, int block_n,
+                                                     int seqlen_kv, int* t0, int* t1) {
+  const int first = z * bpc + (z < extra ? z : extra);
+  const int ntiles = bpc + (z < extra ? 1 : 0);
+  long long a = (long long)first * block_n;
+  long long e = a + (long long)ntiles * block_n;
+  if (a > seqlen_kv) a = seqlen_kv;
+  if (e > seqlen_kv) e = seqlen_kv;
+  *t0 = (int)a;
+  *t1 = (int)e;
+}
+
+// ---------------------------------------------------------------------------
+// host-side error text (thread local, read through mla_last_error)
+// ---------------------------------------------------------------------------
+void set_error(const char* fmt, ...);
+
+// ---------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------
+struct DecodeArgs {
+  const void* q;
+  const void* q_pe;
+  const void* kv;
+  const void* k_pe;
+  void* out;          // final output (used when ns == 1)
+  float* lse;         // optional final lse (natural log)
+  float* part_o;      // [ns, batch, heads, 512]
+  float* part_lse;    // [ns, batch, heads]
+  int batch, heads, seqlen_kv, dtype;
+  float softmax_scale;  // multiplies raw scores
+  SplitPlan plan;
+  cudaStream_t stream;
+};
+
+// CUDA-core split-KV kernel (mla_simt.cu).  Returns a cudaError_t.
+cudaError_t launch_simt_decode(const DecodeArgs& a);
+int simt_block_n();                       // KV rows per tile of the SIMT kernel
+int simt_ctas_per_sm();                   // resident CTAs per SM (occupancy target)
+
+// LSE combine (mla_combine.cu).
+cudaError_t launch_combine(const float* part_lse, const float* part_o, int ns, int batch,
+                           int heads, void* out, float* lse, int dtype, cudaStream_t stream);
+
+}  // namespace mla

@@ -1,0 +1,17 @@
+// Interface of the tcgen05/TMA/TMEM decode kernel (mla_sm100.cu).
+#pragma once
+
+#include "mla_common.cuh"
+
+namespace mla {
+
+// True when the tensor-core kernel covers this shape.
+bool sm100_supports(int heads, int seqlen_kv);
+
+// Split plan (and kernel variant) the tensor-core kernel uses for this shape.
+SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int* variant);
+
+// Enqueue the tensor-core split-KV kernel; partials go to a.part_o/a.part_lse.
+cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant);
+
+}  // namespace mla

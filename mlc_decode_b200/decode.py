@@ -1,0 +1,166 @@
+"""Host side of the decode path: the callable kernel object and its workspace.
+
+``MlaDecodeKernel`` is what the reference's ``_get_kernel`` /
+``flashattn_shared_q`` return (a TileLang ``JITKernel`` there,
+mla_decode.py:690-710): ``kernel(q, q_pe, kv, k_pe, out)`` writes ``out`` in
+place on the current CUDA stream.  The reference allocates its ``glse`` /
+``output_partial`` scratch inside the kernel on every call
+(mla_decode.py:73-76); here the object owns a workspace per (device, dtype),
+allocated on first use and reused, and passes it through the C ABI.
+"""
+from __future__ import annotations
+
+import os
+import threading
+
+import torch
+
+from . import capi
+
+DIM = 512
+PE_DIM = 64
+_DTYPES = {torch.float16: capi.MLA_DTYPE_F16, torch.bfloat16: capi.MLA_DTYPE_BF16}
+
+
+def _check_tensor(name, t, shape, dtype, device):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (got {t.device})")
+    if device is not None and t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} has dtype {t.dtype}, expected {dtype}")
+    if tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+class MlaDecodeKernel:
+    """Absorbed-MLA decode for one (batch, heads, kv_heads, kv_ctx, dim, pe_dim).
+
+    ``cfg`` is a reference-style config dict (keys block_N, block_H, num_split,
+    spread, num_stages, combine_groups; plus ``kernel`` = "auto"/"simt"/"tc"),
+    or None to let the library choose.  Only the absorbed shape of the
+    reference is accepted: kv_heads == 1, dim == 512, pe_dim == 64
+    (baseline_mla.py:16).
+    """
+
+    def __init__(self, batch, heads, kv_head_num, seqlen_kv, dim=DIM, pe_dim=PE_DIM, cfg=None,
+                 softmax_scale=None):
+        if int(kv_head_num) != 1:
+            raise ValueError(f"kv_head_num must be 1 (absorbed MLA), got {kv_head_num}")
+        if int(dim) != DIM or int(pe_dim) != PE_DIM:
+            raise ValueError(f"dim/pe_dim must be {DIM}/{PE_DIM}, got {dim}/{pe_dim}")
+        if int(batch) < 1 or int(heads) < 1 or int(seqlen_kv) < 1:
+            raise ValueError("batch, heads and seqlen_kv must be >= 1")
+        self.batch, self.heads, self.seqlen_kv = int(batch), int(heads), int(seqlen_kv)
+        self.kv_heads, self.dim, self.pe_dim = 1, DIM, PE_DIM
+        self.cfg = dict(cfg or {})
+        if softmax_scale is not None:
+            self.cfg["softmax_scale"] = float(softmax_scale)
+        self._ccfg = capi.make_cfg(self.cfg)
+        capi.load()   # fail loudly now if the library is unusable
+        self._ws = {}
+        self._lock = threading.Lock()
+
+    # -- workspace ---------------------------------------------------------
+    def workspace_bytes(self, dtype: torch.dtype) -> int:
+        return capi.workspace_bytes(self.batch, self.heads, self.seqlen_kv, _DTYPES[dtype], self._ccfg)
+
+    def _workspace(self, device, dtype):
+        key = (device.index, dtype)
+        ws = self._ws.get(key)
+        if ws is None:
+            with self._lock:
+                ws = self._ws.get(key)
+                if ws is None:
+                    n = self.workspace_bytes(dtype)
+                    ws = torch.empty(max(n, 1), dtype=torch.uint8, device=device)
+                    self._ws[key] = ws
+        return ws
+
+    # -- call ----------------------------------------------------------------
+    def __call__(self, q, q_pe, kv, k_pe, out, lse=None):
+        """Write softmax(([q|q_pe].[kv|k_pe]^T) * scale) . kv into ``out``.
+
+        ``lse`` (optional, float32 [batch, heads]) receives the natural-log
+        log-sum-exp of the scaled scores.
+        """
+        b, h, s = self.batch, self.heads, self.seqlen_kv
+        dtype = q.dtype if isinstance(q, torch.Tensor) else None
+        if dtype not in _DTYPES:
+            raise ValueError(f"q must be float16 or bfloat16, got {dtype}")
+        dev = q.device
+        _check_tensor("q", q, (b, h, DIM), dtype, None)
+        _check_tensor("q_pe", q_pe, (b, h, PE_DIM), dtype, dev)
+        _check_tensor("kv", kv, (b, s, 1, DIM), dtype, dev)
+        _check_tensor("k_pe", k_pe, (b, s, 1, PE_DIM), dtype, dev)
+        _check_tensor("out", out, (b, h, DIM), dtype, dev)
+        lse_ptr = None
+        if lse is not None:
+            _check_tensor("lse", lse, (b, h), torch.float32, dev)
+            lse_ptr = lse.data_ptr()
+        ws = self._workspace(dev, dtype)
+        with torch.cuda.device(dev):
+            stream = torch.cuda.current_stream(dev).cuda_stream
+        capi.decode_fwd(q.data_ptr(), q_pe.data_ptr(), kv.data_ptr(), k_pe.data_ptr(), out.data_ptr(),
+                        lse_ptr, ws.data_ptr(), ws.numel(), b, h, s, _DTYPES[dtype], self._ccfg, stream)
+
+    def splitkv(self, q, q_pe, kv, k_pe, out, lse=None):
+        """First launch of a call only (the split-KV kernel); pair with ``combine_ws``.
+
+        Device pointers and shapes are trusted to match a previous checked call.
+        """
+        ws = self._workspace(q.device, q.dtype)
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        capi.decode_splitkv(q.data_ptr(), q_pe.data_ptr(), kv.data_ptr(), k_pe.data_ptr(), out.data_ptr(),
+                            None if lse is None else lse.data_ptr(), ws.data_ptr(), ws.numel(),
+                            self.batch, self.heads, self.seqlen_kv, _DTYPES[q.dtype], self._ccfg, stream)
+
+    def combine_ws(self, out, lse=None):
+        """Second launch of a call: combine the partials ``splitkv`` left in the workspace."""
+        ws = self._workspace(out.device, out.dtype)
+        stream = torch.cuda.current_stream(out.device).cuda_stream
+        capi.decode_combine_ws(out.data_ptr(), None if lse is None else lse.data_ptr(), ws.data_ptr(),
+                               ws.numel(), self.batch, self.heads, self.seqlen_kv, _DTYPES[out.dtype],
+                               self._ccfg, stream)
+
+    def launches_per_call(self, dtype=torch.bfloat16) -> int:
+        """Kernels one call enqueues (1 for a single-split plan, else 2)."""
+        return 2 if self.workspace_bytes(dtype) > 0 else 1
+
+    def get_kernel_source(self) -> str:
+        """CUDA source of the kernels this object launches (cf. dump_kernel_src.py:40)."""
+        here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "csrc")
+        parts = []
+        for name in ("mla_sm100.cu", "mla_simt.cu", "mla_combine.cu"):
+            with open(os.path.join(here, name)) as f:
+                parts.append(f"// ===== {name} =====\n" + f.read())
+        return "\n".join(parts)
+
+    def __repr__(self):
+        return (f"MlaDecodeKernel(batch={self.batch}, heads={self.heads}, seqlen_kv={self.seqlen_kv}, "
+                f"cfg={self.cfg})")
+
+
+def combine(part_lse: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor, lse=None):
+    """LSE-merge ``num_split`` normalised partials (split-major) into ``out``.
+
+    part_lse float32 [ns, b, h] (natural log), part_o float32 [ns, b, h, 512].
+    """
+    ns, b, h = part_lse.shape
+    _check_tensor("part_lse", part_lse, (ns, b, h), torch.float32, None)
+    _check_tensor("part_o", part_o, (ns, b, h, DIM), torch.float32, part_lse.device)
+    if out.dtype not in _DTYPES:
+        raise ValueError("out must be float16 or bfloat16")
+    _check_tensor("out", out, (b, h, DIM), out.dtype, part_lse.device)
+    lse_ptr = None
+    if lse is not None:
+        _check_tensor("lse", lse, (b, h), torch.float32, part_lse.device)
+        lse_ptr = lse.data_ptr()
+    with torch.cuda.device(part_lse.device):
+        stream = torch.cuda.current_stream(part_lse.device).cuda_stream
+    capi.combine(part_lse.data_ptr(), part_o.data_ptr(), ns, b, h, out.data_ptr(), lse_ptr,
+                 _DTYPES[out.dtype], stream)
