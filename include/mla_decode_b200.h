@@ -84,7 +84,9 @@ int32_t mla_split_plan(int32_t seqlen_kv, int32_t num_split, int32_t block_n,
  * Bytes of device scratch mla_decode_fwd needs for this shape and config
  * (partial O and partial LSE per split, float32).  Replaces the per-call
  * T.alloc_global of glse / output_partial (mla_decode.py:73-76).
- * Returns 0 on a bad argument (see mla_last_error).
+ * Clears this thread's error text on entry; returns 0 either when no
+ * workspace is needed (error text stays empty) or on a bad argument (error
+ * text set, see mla_last_error).
  */
 size_t mla_workspace_bytes(int32_t batch, int32_t heads, int32_t seqlen_kv,
                            int32_t dtype, const MlaCfg* cfg);

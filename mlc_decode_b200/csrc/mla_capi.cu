@@ -134,6 +134,7 @@ int32_t mla_split_plan(int32_t seqlen_kv, int32_t num_split, int32_t block_n, in
 
 size_t mla_workspace_bytes(int32_t batch, int32_t heads, int32_t seqlen_kv, int32_t dtype,
                            const MlaCfg* cfg) {
+  g_last_error.clear();   // a 0 result with no error text means "no workspace needed"
   if (check_shape(batch, heads, seqlen_kv, dtype) != MLA_OK) return 0;
   Resolved r{};
   if (resolve(batch, heads, seqlen_kv, cfg, &r) != MLA_OK) return 0;
