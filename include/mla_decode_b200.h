@@ -138,6 +138,27 @@ int32_t mla_combine(const float* part_lse, const float* part_o,
                     int32_t num_split, int32_t batch, int32_t heads,
                     void* out, float* lse, int32_t dtype, void* stream);
 
+/*
+ * mla_decode_fwd without a workspace argument, for callers that cannot
+ * allocate device memory where they decode (code running under CUDA-graph
+ * capture, servers that reserve all memory up front and forbid allocation on
+ * the serving path, plugin hosts whose memory another runtime owns).  No
+ * counterpart in the reference: it always allocates its scratch per call.
+ *
+ * Same inputs, outputs, checks and result as mla_decode_fwd; the split-KV
+ * scratch comes from a static device array of MLA_NOALLOC_SCRATCH_BYTES that
+ * every GPU loading the library holds until exit.  Shapes whose
+ * mla_workspace_bytes exceeds it return MLA_ERR_WORKSPACE.  The first call on
+ * a device looks up the array's address (cudaGetSymbolAddress); make it
+ * before any stream capture.  All calls share the array: calls that overlap
+ * on the GPU race.  Allocates nothing.
+ */
+#define MLA_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+int32_t mla_decode_fwd_noalloc(const void* q, const void* q_pe, const void* kv,
+                               const void* k_pe, void* out, float* lse,
+                               int32_t batch, int32_t heads, int32_t seqlen_kv,
+                               int32_t dtype, const MlaCfg* cfg, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

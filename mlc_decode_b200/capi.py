@@ -23,7 +23,7 @@ STATUS_NAMES = {0: "MLA_OK", 1: "MLA_ERR_ARG", 2: "MLA_ERR_WORKSPACE", 3: "MLA_E
 
 EXPORTED_SYMBOLS = ("mla_abi_version", "mla_last_error", "mla_split_plan",
                     "mla_workspace_bytes", "mla_decode_fwd", "mla_decode_splitkv",
-                    "mla_decode_combine_ws", "mla_combine")
+                    "mla_decode_combine_ws", "mla_combine", "mla_decode_fwd_noalloc")
 
 
 class MlaCfg(ctypes.Structure):
@@ -84,6 +84,9 @@ def load(build_if_missing: bool = True):
         lib.mla_decode_combine_ws.argtypes = [vp, vp, vp, sz, i32, i32, i32, i32,
                                               ctypes.POINTER(MlaCfg), vp]
         lib.mla_decode_combine_ws.restype = i32
+        lib.mla_decode_fwd_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32,
+                                               ctypes.POINTER(MlaCfg), vp]
+        lib.mla_decode_fwd_noalloc.restype = i32
         lib.mla_combine.argtypes = [vp, vp, i32, i32, i32, vp, vp, i32, vp]
         lib.mla_combine.restype = i32
         _lib = lib
@@ -137,6 +140,13 @@ def decode_fwd(q, q_pe, kv, k_pe, out, lse, ws, ws_bytes, batch, heads, seqlen_k
     """Raw pointers in, status checked.  Pointers are ints (device addresses)."""
     check(load().mla_decode_fwd(q, q_pe, kv, k_pe, out, lse, ws, ws_bytes, int(batch), int(heads),
                                 int(seqlen_kv), int(dtype), ctypes.byref(cfg), stream))
+
+
+def decode_fwd_noalloc(q, q_pe, kv, k_pe, out, lse, batch, heads, seqlen_kv, dtype, cfg: MlaCfg,
+                       stream) -> None:
+    """mla_decode_fwd_noalloc: scratch from the library's static device array (no allocation)."""
+    check(load().mla_decode_fwd_noalloc(q, q_pe, kv, k_pe, out, lse, int(batch), int(heads),
+                                        int(seqlen_kv), int(dtype), ctypes.byref(cfg), stream))
 
 
 def decode_splitkv(q, q_pe, kv, k_pe, out, lse, ws, ws_bytes, batch, heads, seqlen_kv, dtype,
