@@ -102,10 +102,20 @@ int resolve(int batch, int heads, int seqlen_kv, const MlaCfg* cfg, Resolved* r)
   return MLA_OK;
 }
 
+// Workspace layout: [status word, 256 B; tensor-core kernel only]
+//                   [partial LSE float32 x rows, padded to 256 B][partial O float32 x rows x 512]
+// (the partial blocks only when the plan needs a combine launch).
+constexpr size_t kStatusBytes = 256;
+
+size_t part_rows(int batch, int heads, const Resolved& r) {
+  return r.plan.part_rows > 0 ? (size_t)r.plan.part_rows : (size_t)r.plan.ns * batch * heads;
+}
+
 size_t workspace_for(int batch, int heads, const Resolved& r) {
-  if (r.kernel == MLA_KERNEL_SIMT && r.plan.ns == 1) return 0;
-  const size_t rows = (size_t)r.plan.ns * batch * heads;
-  return align_up(rows * sizeof(float), 256) + rows * kDim * sizeof(float);
+  const size_t head = r.kernel == MLA_KERNEL_TC ? kStatusBytes : 0;
+  if (!r.plan.needs_combine) return head;
+  const size_t rows = part_rows(batch, heads, r);
+  return head + align_up(rows * sizeof(float), 256) + rows * kDim * sizeof(float);
 }
 
 }  // namespace
@@ -192,10 +202,16 @@ int prepare(const char* fn, const void* q, const void* q_pe, const void* kv, con
   a->plan = r->plan;
   a->stream = static_cast<cudaStream_t>(stream);
   if (*need > 0) {
-    const size_t rows = (size_t)r->plan.ns * batch * heads;
-    a->part_lse = static_cast<float*>(const_cast<void*>(workspace));
-    a->part_o = reinterpret_cast<float*>(static_cast<char*>(const_cast<void*>(workspace)) +
-                                         align_up(rows * sizeof(float), 256));
+    char* base = static_cast<char*>(const_cast<void*>(workspace));
+    if (r->kernel == MLA_KERNEL_TC) {
+      a->status = reinterpret_cast<uint32_t*>(base);
+      base += kStatusBytes;
+    }
+    if (r->plan.needs_combine) {
+      const size_t rows = part_rows(batch, heads, *r);
+      a->part_lse = reinterpret_cast<float*>(base);
+      a->part_o = reinterpret_cast<float*>(base + align_up(rows * sizeof(float), 256));
+    }
   }
   return MLA_OK;
 }
@@ -210,10 +226,13 @@ int run_splitkv(const char* fn, const DecodeArgs& a, const Resolved& r) {
   return MLA_OK;
 }
 
-int run_combine_ws(const char* fn, const DecodeArgs& a, const Resolved& r, size_t need) {
-  if (need == 0) return MLA_OK;   // single-split plan: the decode kernel wrote out/lse
-  const cudaError_t err = launch_combine(a.part_lse, a.part_o, r.plan.ns, a.batch, a.heads, a.out,
-                                         a.lse, a.dtype, a.stream);
+int run_combine_ws(const char* fn, const DecodeArgs& a, const Resolved& r) {
+  if (!r.plan.needs_combine) return MLA_OK;   // the decode kernel wrote out/lse itself
+  const cudaError_t err =
+      r.kernel == MLA_KERNEL_TC
+          ? launch_sm100_combine(a)
+          : launch_combine(a.part_lse, a.part_o, r.plan.ns, a.batch, a.heads, a.out, a.lse, a.dtype,
+                           a.stream);
   if (err != cudaSuccess) {
     set_error("%s: combine launch failed: %s", fn, cudaGetErrorString(err));
     return MLA_ERR_CUDA;
@@ -238,7 +257,7 @@ int32_t mla_decode_fwd(const void* q, const void* q_pe, const void* kv, const vo
   if (rc != MLA_OK) return rc;
   rc = run_splitkv("mla_decode_fwd", a, r);
   if (rc != MLA_OK) return rc;
-  return run_combine_ws("mla_decode_fwd", a, r, need);
+  return run_combine_ws("mla_decode_fwd", a, r);
 }
 
 int32_t mla_decode_splitkv(const void* q, const void* q_pe, const void* kv, const void* k_pe,
@@ -265,7 +284,7 @@ int32_t mla_decode_combine_ws(void* out, float* lse, const void* workspace, size
                          workspace, workspace_bytes, batch, heads, seqlen_kv, dtype, cfg, stream,
                          false, &a, &r, &need);
   if (rc != MLA_OK) return rc;
-  return run_combine_ws("mla_decode_combine_ws", a, r, need);
+  return run_combine_ws("mla_decode_combine_ws", a, r);
 }
 
 int32_t mla_combine(const float* part_lse, const float* part_o, int32_t num_split, int32_t batch,

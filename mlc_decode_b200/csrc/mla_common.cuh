@@ -51,10 +51,12 @@ template <> struct Elt<__nv_bfloat16> {
 // split planner: _split_plan (mla_decode.py:9-30)
 // ---------------------------------------------------------------------------
 struct SplitPlan {
-  int ns;            // number of splits actually used
-  int bpc;           // KV tiles per split
-  int extra;         // the first `extra` splits take one more tile
+  int ns;            // number of splits actually used (partial slots)
+  int bpc;           // KV tiles per split (tensor-core plan: CTA pairs)
+  int extra;         // the first `extra` splits take one more tile (tensor-core plan: slots per pair)
   int block_n;       // KV rows per tile
+  long long part_rows;   // partial rows in the workspace (0: derive from ns x batch x heads)
+  bool needs_combine;    // a second (combine) launch is needed
 };
 
 inline SplitPlan split_plan(int seqlen_kv, int num_split, int block_n, bool spread) {
@@ -75,6 +77,8 @@ inline SplitPlan split_plan(int seqlen_kv, int num_split, int block_n, bool spre
     p.bpc = nb / p.ns;
     p.extra = nb % p.ns;
   }
+  p.part_rows = 0;
+  p.needs_combine = p.ns > 1;
   return p;
 }
 
@@ -109,6 +113,7 @@ struct DecodeArgs {
   float* lse;         // optional final lse (natural log)
   float* part_o;      // [ns, batch, heads, 512]
   float* part_lse;    // [ns, batch, heads]
+  uint32_t* status;   // workspace status word (tensor-core kernel), nullable
   int batch, heads, seqlen_kv, dtype;
   float softmax_scale;  // multiplies raw scores
   SplitPlan plan;

@@ -77,7 +77,8 @@ class MlaDecodeKernel:
                 ws = self._ws.get(key)
                 if ws is None:
                     n = self.workspace_bytes(dtype)
-                    ws = torch.empty(max(n, 1), dtype=torch.uint8, device=device)
+                    # zeroed once: the first word is the kernels' status word
+                    ws = torch.zeros(max(n, 1), dtype=torch.uint8, device=device)
                     self._ws[key] = ws
         return ws
 
@@ -126,6 +127,13 @@ class MlaDecodeKernel:
         capi.decode_combine_ws(out.data_ptr(), None if lse is None else lse.data_ptr(), ws.data_ptr(),
                                ws.numel(), self.batch, self.heads, self.seqlen_kv, _DTYPES[out.dtype],
                                self._ccfg, stream)
+
+    def device_status(self, device, dtype) -> int:
+        """Status word the tensor-core kernel leaves in the workspace (0 = no timeout)."""
+        ws = self._ws.get((torch.device(device).index, dtype))
+        if ws is None or ws.numel() < 4:
+            return 0
+        return int(ws[:4].view(torch.int32).item())
 
     def launches_per_call(self, dtype=torch.bfloat16) -> int:
         """Kernels one call enqueues (1 for a single-split plan, else 2)."""
