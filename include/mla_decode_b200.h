@@ -92,6 +92,19 @@ size_t mla_workspace_bytes(int32_t batch, int32_t heads, int32_t seqlen_kv,
                            int32_t dtype, const MlaCfg* cfg);
 
 /*
+ * Facts about the plan mla_decode_fwd would use for this shape and config:
+ *   out4[0] kernel (enum MlaKernelKind, never AUTO)
+ *   out4[1] KV splits per sequence (CUDA-core kernel) or CTA pairs (tensor-core kernel)
+ *   out4[2] kernel launches per call (1 or 2)
+ *   out4[3] bytes at the start of the workspace that must be zero before the
+ *           first call with it (the tensor-core kernel's status word and piece
+ *           counters; every call leaves them zero again)
+ * Mirrors the reference's split planning (mla_decode.py:9-30, 539-606).
+ */
+int32_t mla_describe_plan(int32_t batch, int32_t heads, int32_t seqlen_kv,
+                          int32_t dtype, const MlaCfg* cfg, int64_t* out4);
+
+/*
  * One decode call: the split-KV main kernel then the LSE combine kernel,
  * enqueued on `stream`.  Replaces the TileLang prim_func `main`
  * (mla_decode.py:65-259) that kernel(q, q_pe, kv, k_pe, out) launches, and the

@@ -23,7 +23,8 @@ STATUS_NAMES = {0: "MLA_OK", 1: "MLA_ERR_ARG", 2: "MLA_ERR_WORKSPACE", 3: "MLA_E
 
 EXPORTED_SYMBOLS = ("mla_abi_version", "mla_last_error", "mla_split_plan",
                     "mla_workspace_bytes", "mla_decode_fwd", "mla_decode_splitkv",
-                    "mla_decode_combine_ws", "mla_combine", "mla_decode_fwd_noalloc")
+                    "mla_decode_combine_ws", "mla_combine", "mla_decode_fwd_noalloc",
+                    "mla_describe_plan")
 
 
 class MlaCfg(ctypes.Structure):
@@ -87,6 +88,9 @@ def load(build_if_missing: bool = True):
         lib.mla_decode_fwd_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32,
                                                ctypes.POINTER(MlaCfg), vp]
         lib.mla_decode_fwd_noalloc.restype = i32
+        lib.mla_describe_plan.argtypes = [i32, i32, i32, i32, ctypes.POINTER(MlaCfg),
+                                           ctypes.POINTER(ctypes.c_int64)]
+        lib.mla_describe_plan.restype = i32
         lib.mla_combine.argtypes = [vp, vp, i32, i32, i32, vp, vp, i32, vp]
         lib.mla_combine.restype = i32
         _lib = lib
@@ -124,6 +128,17 @@ def split_plan(seqlen_kv: int, num_split: int, block_n: int, spread: bool = Fals
     out = (ctypes.c_int32 * 3)()
     check(load().mla_split_plan(int(seqlen_kv), int(num_split), int(block_n), int(bool(spread)), out))
     return int(out[0]), int(out[1]), int(out[2])
+
+
+KERNEL_NAMES = {MLA_KERNEL_SIMT: "simt", MLA_KERNEL_TC: "tc"}
+
+
+def describe_plan(batch, heads, seqlen_kv, dtype, cfg: MlaCfg) -> dict:
+    """mla_describe_plan: kernel, splits/pairs, launches per call, zero-prefix bytes."""
+    out = (ctypes.c_int64 * 4)()
+    check(load().mla_describe_plan(int(batch), int(heads), int(seqlen_kv), int(dtype), ctypes.byref(cfg), out))
+    return {"kernel": KERNEL_NAMES.get(int(out[0]), int(out[0])), "splits": int(out[1]),
+            "launches": int(out[2]), "zero_prefix_bytes": int(out[3])}
 
 
 def workspace_bytes(batch, heads, seqlen_kv, dtype, cfg: MlaCfg) -> int:

@@ -102,17 +102,23 @@ int resolve(int batch, int heads, int seqlen_kv, const MlaCfg* cfg, Resolved* r)
   return MLA_OK;
 }
 
-// Workspace layout: [status word, 256 B; tensor-core kernel only]
-//                   [partial LSE float32 x rows, padded to 256 B][partial O float32 x rows x 512]
-// (the partial blocks only when the plan needs a combine launch).
+// Workspace layout:
+//   tensor-core kernel: [status word, 256 B][piece counters uint32 x batch x 2, padded to 256 B]
+//                       [partial LSE float32 x rows, padded to 256 B][partial O float32 x rows x 512]
+//                       (partials only when some sequence is split between CTA pairs)
+//   CUDA-core kernel:   [partial LSE][partial O] when the plan has more than one split
+// The tensor-core kernel's counters must be zero before the first call (a zero-filled
+// workspace); every call leaves them zero again.
 constexpr size_t kStatusBytes = 256;
+
+size_t counter_bytes(int batch) { return align_up((size_t)batch * 2 * sizeof(uint32_t), 256); }
 
 size_t part_rows(int batch, int heads, const Resolved& r) {
   return r.plan.part_rows > 0 ? (size_t)r.plan.part_rows : (size_t)r.plan.ns * batch * heads;
 }
 
 size_t workspace_for(int batch, int heads, const Resolved& r) {
-  const size_t head = r.kernel == MLA_KERNEL_TC ? kStatusBytes : 0;
+  const size_t head = r.kernel == MLA_KERNEL_TC ? kStatusBytes + counter_bytes(batch) : 0;
   if (!r.plan.needs_combine) return head;
   const size_t rows = part_rows(batch, heads, r);
   return head + align_up(rows * sizeof(float), 256) + rows * kDim * sizeof(float);
@@ -139,6 +145,25 @@ int32_t mla_split_plan(int32_t seqlen_kv, int32_t num_split, int32_t block_n, in
   out3[0] = p.ns;
   out3[1] = p.bpc;
   out3[2] = p.extra;
+  return MLA_OK;
+}
+
+int32_t mla_describe_plan(int32_t batch, int32_t heads, int32_t seqlen_kv, int32_t dtype,
+                          const MlaCfg* cfg, int64_t* out4) {
+  if (out4 == nullptr) {
+    set_error("mla_describe_plan: null output");
+    return MLA_ERR_ARG;
+  }
+  int rc = check_shape(batch, heads, seqlen_kv, dtype);
+  if (rc != MLA_OK) return rc;
+  Resolved r{};
+  rc = resolve(batch, heads, seqlen_kv, cfg, &r);
+  if (rc != MLA_OK) return rc;
+  const bool tc = r.kernel == MLA_KERNEL_TC;
+  out4[0] = r.kernel;
+  out4[1] = tc ? r.plan.bpc : r.plan.ns;
+  out4[2] = (!tc && r.plan.needs_combine) ? 2 : 1;
+  out4[3] = tc ? (int64_t)(kStatusBytes + counter_bytes(batch)) : 0;
   return MLA_OK;
 }
 
@@ -205,7 +230,8 @@ int prepare(const char* fn, const void* q, const void* q_pe, const void* kv, con
     char* base = static_cast<char*>(const_cast<void*>(workspace));
     if (r->kernel == MLA_KERNEL_TC) {
       a->status = reinterpret_cast<uint32_t*>(base);
-      base += kStatusBytes;
+      a->counters = reinterpret_cast<uint32_t*>(base + kStatusBytes);
+      base += kStatusBytes + counter_bytes(batch);
     }
     if (r->plan.needs_combine) {
       const size_t rows = part_rows(batch, heads, *r);
@@ -227,12 +253,11 @@ int run_splitkv(const char* fn, const DecodeArgs& a, const Resolved& r) {
 }
 
 int run_combine_ws(const char* fn, const DecodeArgs& a, const Resolved& r) {
-  if (!r.plan.needs_combine) return MLA_OK;   // the decode kernel wrote out/lse itself
-  const cudaError_t err =
-      r.kernel == MLA_KERNEL_TC
-          ? launch_sm100_combine(a)
-          : launch_combine(a.part_lse, a.part_o, r.plan.ns, a.batch, a.heads, a.out, a.lse, a.dtype,
-                           a.stream);
+  // the decode kernel wrote out/lse itself: single-split plans, and the tensor-core
+  // kernel, whose epilogue merges split sequences
+  if (!r.plan.needs_combine || r.kernel == MLA_KERNEL_TC) return MLA_OK;
+  const cudaError_t err = launch_combine(a.part_lse, a.part_o, r.plan.ns, a.batch, a.heads, a.out,
+                                         a.lse, a.dtype, a.stream);
   if (err != cudaSuccess) {
     set_error("%s: combine launch failed: %s", fn, cudaGetErrorString(err));
     return MLA_ERR_CUDA;

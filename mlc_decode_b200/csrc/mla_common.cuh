@@ -114,6 +114,7 @@ struct DecodeArgs {
   float* part_o;      // [ns, batch, heads, 512]
   float* part_lse;    // [ns, batch, heads]
   uint32_t* status;   // workspace status word (tensor-core kernel), nullable
+  uint32_t* counters; // per-(sequence, CTA rank) piece counters (tensor-core kernel)
   int batch, heads, seqlen_kv, dtype;
   float softmax_scale;  // multiplies raw scores
   SplitPlan plan;

@@ -20,10 +20,12 @@
 //    cudaGetSymbolAddress (once per device, with that device current).  Make
 //    that first call before any stream capture begins.
 //  * All calls share the one array, which keeps the last call's contents.
-//    The decode kernels overwrite every scratch entry they later read, so
-//    nothing needs clearing; but two calls whose kernels overlap on the GPU
-//    (different streams without ordering between them) race on the array and
-//    both results are undefined.  Serialise such calls on one stream.
+//    The bytes the kernels need zeroed on entry (the tensor-core kernel's status
+//    word and piece counters, mla_describe_plan out4[3]) are cleared with a
+//    cudaMemsetAsync on the caller's stream before each launch; everything else
+//    is overwritten before it is read.  Two calls whose kernels overlap on the
+//    GPU (different streams without ordering between them) race on the array
+//    and both results are undefined.  Serialise such calls on one stream.
 //  * Nothing here calls cudaMalloc, cudaFree or an allocating library routine.
 #include <mutex>
 
@@ -89,8 +91,22 @@ int32_t mla_decode_fwd_noalloc(const void* q, const void* q_pe, const void* kv, 
     return MLA_ERR_WORKSPACE;
   }
   void* scratch = nullptr;
-  const int rc = mla::scratch_address(&scratch);
+  int rc = mla::scratch_address(&scratch);
   if (rc != MLA_OK) return rc;
+  // The array keeps whatever the previous call left; the part the kernels need
+  // zeroed on entry (tensor-core status word and piece counters) is cleared here.
+  int64_t info[4];
+  rc = mla_describe_plan(batch, heads, seqlen_kv, dtype, cfg, info);
+  if (rc != MLA_OK) return rc;
+  if (info[3] > 0) {
+    const cudaError_t err =
+        cudaMemsetAsync(scratch, 0, (size_t)info[3], static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) {
+      mla::set_error("mla_decode_fwd_noalloc: clearing the scratch header failed: %s",
+                     cudaGetErrorString(err));
+      return MLA_ERR_CUDA;
+    }
+  }
   return mla_decode_fwd(q, q_pe, kv, k_pe, out, lse, scratch, mla::kNoAllocScratchBytes, batch,
                         heads, seqlen_kv, dtype, cfg, stream);
 }

@@ -55,13 +55,22 @@ constexpr int kHeads = 128;           // heads per CTA pair
 constexpr int kTile = 128;            // KV rows per tile
 constexpr uint32_t kStageBytes = 16384;
 constexpr uint32_t kChunkBytes = 8192;       // one 64 x 128 B swizzled box
-constexpr uint32_t kQBytes = 9 * kChunkBytes;
+// Q rows in shared memory: latent dims [256, 512) (4 boxes) and the rope dims (1 box);
+// latent dims [0, 256) live in TMEM as the A operand of the first 16 QK^T k-steps.
+constexpr int kQTDims = 256;
+constexpr uint32_t kQBytes = 5 * kChunkBytes;
 constexpr uint32_t kPBytes = 2 * kChunkBytes;   // one P operand: 64 rows x 128 tokens
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 128;
+constexpr uint32_t kColQT = 384;      // Q dims [0, 256) as bf16/fp16 pairs: 128 columns
 constexpr int kThreads = 256;
 constexpr float kRescaleLog2 = 8.0f;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr int kPrefetchTiles = 2;
+// A merge stages another pair's 64 partial rows (fp32, 2 KB each) in shared memory
+// at this row pitch (16 bytes of padding: threads reading one column of 32 rows
+// hit distinct banks).
+constexpr uint32_t kMergePitch = kDim * 4 + 16;     // L2 prefetch distance of the K producer, in tiles (0: off)
 
 // status codes written to the workspace status word on a timeout
 constexpr uint32_t kErrKLoad = 0x101, kErrVLoad = 0x102, kErrQK = 0x103, kErrPV = 0x104,
@@ -82,18 +91,18 @@ template <>
 struct Cfg<__half> {
   static constexpr uint32_t kFmt = 0;
   static constexpr int kPParts = 1;
-  static constexpr int kKStages = 5;
+  static constexpr int kKStages = 6;
   static constexpr int kVStages = 3;
 };
 
 struct Barriers {
   uint64_t kfull[8], kempty[8];
   uint64_t vfull[8], vempty[8];
-  uint64_t q_full, q_empty;
+  uint64_t q_full, q_empty, qt_full;
   uint64_t s_full[2], s_free[2];
-  uint64_t p_full;
+  uint64_t p_full[2];
   uint64_t xchg[2];
-  uint64_t o_done, o_free, lx;
+  uint64_t o_done[2], o_free, lx, mg, mg2, mload, mdone;
   uint64_t drain_qk, drain_pv;
 };
 static_assert(sizeof(Barriers) <= 512, "barrier block");
@@ -103,7 +112,8 @@ template <typename T>
 struct Smem {
   static constexpr uint32_t kQ = 0;
   static constexpr uint32_t kP = kQ + kQBytes;
-  static constexpr uint32_t kKRing = kP + Cfg<T>::kPParts * kPBytes;
+  static constexpr uint32_t kPBuf = Cfg<T>::kPParts * kPBytes;     // one P buffer (hi [, lo])
+  static constexpr uint32_t kKRing = kP + 2 * kPBuf;
   static constexpr uint32_t kVRing = kKRing + Cfg<T>::kKStages * kStageBytes;
   static constexpr uint32_t kBar = kVRing + Cfg<T>::kVStages * kStageBytes;
   static constexpr uint32_t kXmax = kBar + 512;
@@ -118,11 +128,16 @@ struct Params {
   CUtensorMap tm_kpe;   // [b*s, 64]
   CUtensorMap tm_q;     // [b*128, 512]
   CUtensorMap tm_qpe;   // [b*128, 64]
+  const uint8_t* kv;    // raw rows, for L2 prefetch
+  const uint8_t* kpe;
+  const uint8_t* q;     // raw Q rows, for the TMEM copy of dims [0, 256)
+  const uint8_t* qpe;
   void* out;
   float* lse_out;
   float* part_o;
   float* part_lse;
   uint32_t* status;
+  uint32_t* counters;   // [batch][2] pieces finished per (sequence, CTA rank); zero between calls
   long long total_tiles;
   int batch, seqlen, nt, pairs, maxp;
   float sl2;            // softmax scale * log2(e)
@@ -140,9 +155,8 @@ __device__ __forceinline__ void raise_abort(const Ctx& c, uint32_t code) {
   if (c.status != nullptr) atomicCAS(c.status, 0u, code);
 }
 
-// Bounded wait for the phase of `parity` on a local barrier.
-__device__ __noinline__ bool wait_bar(const Ctx& c, uint32_t bar, uint32_t parity, uint32_t code) {
-  if (ptx::mbar_try_wait(bar, parity)) return true;
+// Slow path of wait_bar: poll with a time limit.
+__device__ __noinline__ bool wait_bar_slow(const Ctx& c, uint32_t bar, uint32_t parity, uint32_t code) {
   const uint64_t t0 = ptx::globaltimer();
   for (;;) {
 #pragma unroll 1
@@ -154,6 +168,11 @@ __device__ __noinline__ bool wait_bar(const Ctx& c, uint32_t bar, uint32_t parit
       return false;
     }
   }
+}
+
+// Bounded wait for the phase of `parity` on a local barrier.
+__device__ __forceinline__ bool wait_bar(const Ctx& c, uint32_t bar, uint32_t parity, uint32_t code) {
+  return ptx::mbar_try_wait(bar, parity) || wait_bar_slow(c, bar, parity, code);
 }
 
 __device__ __forceinline__ bool aborted(const Ctx& c) {
@@ -201,6 +220,20 @@ struct Ring {
   }
 };
 
+// Pull this CTA's 64 rows of flattened tile `t` (latent 64 KB, rope 8 KB, both
+// contiguous) into L2, so that the TMA loads of that tile later hit L2: this keeps
+// enough bytes in flight to HBM without spending shared memory on deeper rings.
+__device__ __forceinline__ void prefetch_tile(const Params& p, long long t, uint32_t rank) {
+  const int bb = (int)(t / p.nt);
+  const int jj = (int)(t - (long long)bb * p.nt);
+  const long long row0 = (long long)bb * p.seqlen + (long long)jj * kTile + 64 * (int)rank;
+  const long long rows = (long long)bb * p.seqlen + p.seqlen - row0;
+  if (rows <= 0) return;
+  const uint32_t n = rows < 64 ? (uint32_t)rows : 64u;
+  ptx::prefetch_l2(p.kv + row0 * (kDim * 2), n * (kDim * 2));
+  ptx::prefetch_l2(p.kpe + row0 * (kPeDim * 2), n * (kPeDim * 2));
+}
+
 // ---------------------------------------------------------------------------
 // K producer: Q once per piece, then per tile 4 latent units + 1 rope unit.
 // ---------------------------------------------------------------------------
@@ -213,23 +246,17 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
   const uint32_t kfull0 = ptx::smem_u32(&bars->kfull[0]);
   const uint32_t kfull0_leader = ptx::mapa(kfull0, 0);
   const uint32_t kempty0 = ptx::smem_u32(&bars->kempty[0]);
-  const uint32_t q_full = ptx::smem_u32(&bars->q_full);
-  const uint32_t q_full_leader = ptx::mapa(q_full, 0);
-  const uint32_t q_empty = ptx::smem_u32(&bars->q_empty);
   Ring<KS> ring;
   PieceIter it(p, pair);
+  const long long t_end = it.t1;
+  long long t_cur = it.t;
+  for (int d = 0; d < kPrefetchTiles && t_cur + d < t_end; ++d) prefetch_tile(p, t_cur + d, rank);
   Piece pc;
-  int piece = 0;
+  // K units stream straight across piece boundaries: Q has its own loader thread
   while (it.next(&pc)) {
-    if (piece > 0 && !wait_bar(c, q_empty, (uint32_t)(piece - 1) & 1u, kErrKLoad)) return;
-    if (leader) ptx::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
-    const int qrow = pc.bb * kHeads + 64 * (int)rank;
 #pragma unroll 1
-    for (int ch = 0; ch < 8; ++ch)
-      ptx::tma_load_2d_pair(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, q_full_leader, 64 * ch, qrow);
-    ptx::tma_load_2d_pair(sbase + S::kQ + 8 * kChunkBytes, &p.tm_qpe, q_full_leader, 0, qrow);
-#pragma unroll 1
-    for (int j = pc.first; j < pc.end; ++j) {
+    for (int j = pc.first; j < pc.end; ++j, ++t_cur) {
+      if (t_cur + kPrefetchTiles < t_end) prefetch_tile(p, t_cur + kPrefetchTiles, rank);
       const int y = pc.bb * p.seqlen + j * kTile + 64 * (int)rank;
 #pragma unroll 1
       for (int u = 0; u < 5; ++u) {
@@ -247,6 +274,49 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
         ring.advance();
       }
     }
+  }
+}
+
+// Pull this CTA's 64 Q rows of sequence `bb` (latent 64 KB, rope 8 KB) into L2.
+__device__ __forceinline__ void prefetch_q(const Params& p, int bb, uint32_t rank) {
+  const long long row0 = (long long)bb * kHeads + 64 * (int)rank;
+  ptx::prefetch_l2(p.q + row0 * (kDim * 2), 64 * (kDim * 2));
+  ptx::prefetch_l2(p.qpe + row0 * (kPeDim * 2), 64 * (kPeDim * 2));
+}
+
+// ---------------------------------------------------------------------------
+// Q loader: per piece, Q dims [256, 512) and the rope dims into shared memory
+// once the previous piece's QK^T no longer reads them; the next piece's rows
+// are pulled into L2 ahead of time (they also feed the TMEM copy).
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void q_loader(const Params& p, const Ctx& c, uint32_t rank, int pair,
+                                         uint32_t sbase, Barriers* bars) {
+  using S = Smem<T>;
+  const bool leader = rank == 0;
+  const uint32_t q_full = ptx::smem_u32(&bars->q_full);
+  const uint32_t q_full_leader = ptx::mapa(q_full, 0);
+  const uint32_t q_empty = ptx::smem_u32(&bars->q_empty);
+  PieceIter it(p, pair);
+  {
+    PieceIter first = it;
+    Piece p0;
+    if (first.next(&p0)) prefetch_q(p, p0.bb, rank);
+  }
+  Piece pc;
+  int piece = 0;
+  while (it.next(&pc)) {
+    PieceIter peek = it;
+    Piece nxt;
+    if (peek.next(&nxt)) prefetch_q(p, nxt.bb, rank);
+    if (piece > 0 && !wait_bar(c, q_empty, (uint32_t)(piece - 1) & 1u, kErrKLoad)) return;
+    if (leader) ptx::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
+    const int qrow = pc.bb * kHeads + 64 * (int)rank;
+#pragma unroll 1
+    for (int ch = 0; ch < 4; ++ch)
+      ptx::tma_load_2d_pair(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, q_full_leader, kQTDims + 64 * ch,
+                            qrow);
+    ptx::tma_load_2d_pair(sbase + S::kQ + 4 * kChunkBytes, &p.tm_qpe, q_full_leader, 0, qrow);
     ++piece;
   }
 }
@@ -300,9 +370,11 @@ __device__ __forceinline__ void qk_issuer(const Params& p, const Ctx& c, int pai
   const uint32_t kempty0 = ptx::smem_u32(&bars->kempty[0]);
   const uint32_t q_full = ptx::smem_u32(&bars->q_full);
   const uint32_t q_empty = ptx::smem_u32(&bars->q_empty);
+  const uint32_t qt_full = ptx::smem_u32(&bars->qt_full);
   const uint32_t s_full0 = ptx::smem_u32(&bars->s_full[0]);
   const uint32_t s_free0 = ptx::smem_u32(&bars->s_free[0]);
-  const uint32_t qbase = sbase + S::kQ;
+  const uint32_t qlo = ptx::sw128_desc_lo(sbase + S::kQ, 16);
+  constexpr uint32_t kHiK = ptx::sw128_desc_hi(1024);
   Ring<KS> ring;
   uint32_t gi = 0;
   PieceIter it(p, pair);
@@ -310,6 +382,7 @@ __device__ __forceinline__ void qk_issuer(const Params& p, const Ctx& c, int pai
   int piece = 0;
   while (it.next(&pc)) {
     if (!wait_bar(c, q_full, (uint32_t)piece & 1u, kErrQK)) return;
+    if (!wait_bar(c, qt_full, (uint32_t)piece & 1u, kErrQK)) return;
     ptx::tc_fence_after();
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j, ++gi) {
@@ -318,18 +391,26 @@ __device__ __forceinline__ void qk_issuer(const Params& p, const Ctx& c, int pai
       if (gi >= 2 && !wait_bar(c, s_free0 + 8 * b, ((gi - 2) >> 1) & 1u, kErrQK)) return;
       ptx::tc_fence_after();
       const uint32_t s_tmem = tmem + 64 * b;
-#pragma unroll 1
+#pragma unroll
       for (int u = 0; u < 5; ++u) {
         if (!wait_bar(c, kfull0 + 8 * ring.stage, ring.phase, kErrQK)) return;
         ptx::tc_fence_after();
-        const uint32_t kb = sbase + S::kKRing + ring.stage * kStageBytes;
-        const int nk = u < 4 ? 8 : 4;
-#pragma unroll 1
-        for (int kk = 0; kk < nk; ++kk) {
-          const int qc = u < 4 ? 2 * u + (kk >> 2) : 8;
-          const uint64_t a = ptx::sw128_desc(qbase + qc * kChunkBytes + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = ptx::sw128_desc(kb + (kk >> 2) * kChunkBytes + (kk & 3) * 32, 16, 1024);
-          ptx::mma_pair_f16(s_tmem, a, bd, kIdesc, (u == 0 && kk == 0) ? 0u : 1u);
+        // descriptor low words; +512 = next 8 KB box, +2 = next 32-byte k-step
+        const uint32_t kb = ptx::sw128_desc_lo(sbase + S::kKRing + ring.stage * kStageBytes, 16);
+        if (u < 2) {
+          // latent dims [0, 256): Q from TMEM, 8 columns (16 elements) per k-step
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            ptx::mma_pair_f16_ts(s_tmem, tmem + kColQT + 8 * (8 * u + kk),
+                                 ptx::make_desc(kb + (kk >> 2) * 512 + (kk & 3) * 2, kHiK), kIdesc,
+                                 (u == 0 && kk == 0) ? 0u : 1u);
+        } else {
+          const uint32_t qa = qlo + (u < 4 ? 2 * (u - 2) : 4) * 512;
+          const int nk = u < 4 ? 8 : 4;
+#pragma unroll
+          for (int kk = 0; kk < nk; ++kk)
+            ptx::mma_pair_f16(s_tmem, ptx::make_desc(qa + (kk >> 2) * 512 + (kk & 3) * 2, kHiK),
+                              ptx::make_desc(kb + (kk >> 2) * 512 + (kk & 3) * 2, kHiK), kIdesc, 1u);
         }
         ptx::mma_commit_pair_mc(kempty0 + 8 * ring.stage, 0x3);
         ring.advance();
@@ -352,9 +433,11 @@ __device__ __forceinline__ void pv_issuer(const Params& p, const Ctx& c, int pai
   constexpr uint32_t kIdesc = ptx::idesc_f16(Cfg<T>::kFmt, 128, 256, 1);
   const uint32_t vfull0 = ptx::smem_u32(&bars->vfull[0]);
   const uint32_t vempty0 = ptx::smem_u32(&bars->vempty[0]);
-  const uint32_t p_full = ptx::smem_u32(&bars->p_full);
-  const uint32_t o_done = ptx::smem_u32(&bars->o_done);
+  const uint32_t p_full0 = ptx::smem_u32(&bars->p_full[0]);
+  const uint32_t o_done0 = ptx::smem_u32(&bars->o_done[0]);
   const uint32_t o_free = ptx::smem_u32(&bars->o_free);
+  const uint32_t plo = ptx::sw128_desc_lo(sbase + S::kP, 16);
+  constexpr uint32_t kHi = ptx::sw128_desc_hi(1024);
   Ring<VS> ring;
   uint32_t gi = 0;
   PieceIter it(p, pair);
@@ -364,7 +447,8 @@ __device__ __forceinline__ void pv_issuer(const Params& p, const Ctx& c, int pai
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j, ++gi) {
       const bool first = j == pc.first;
-      if (!wait_bar(c, p_full, gi & 1u, kErrPV)) return;
+      const uint32_t b = gi & 1u;
+      if (!wait_bar(c, p_full0 + 8 * b, (gi >> 1) & 1u, kErrPV)) return;
       // a new piece restarts O: the previous piece's epilogue must have read it
       if (first && piece > 0 && !wait_bar(c, o_free, (uint32_t)(piece - 1) & 1u, kErrPV)) return;
       ptx::tc_fence_after();
@@ -373,22 +457,21 @@ __device__ __forceinline__ void pv_issuer(const Params& p, const Ctx& c, int pai
         const int nh = u >> 1, th = u & 1;
         if (!wait_bar(c, vfull0 + 8 * ring.stage, ring.phase, kErrPV)) return;
         ptx::tc_fence_after();
-        const uint32_t vb = sbase + S::kVRing + ring.stage * kStageBytes;
+        // descriptor low words: V is MN-major (+128 = next 16 rows), P K-major (+2 = next k-step)
+        const uint32_t vb = ptx::sw128_desc_lo(sbase + S::kVRing + ring.stage * kStageBytes, kChunkBytes);
 #pragma unroll
         for (int part = 0; part < Cfg<T>::kPParts; ++part) {
-          const uint32_t pb = sbase + S::kP + part * kPBytes + th * kChunkBytes;
+          const uint32_t pa = plo + b * (S::kPBuf >> 4) + part * (kPBytes >> 4) + th * 512;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t a = ptx::sw128_desc(pb + kk * 32, 16, 1024);
-            const uint64_t bd = ptx::sw128_desc(vb + kk * 2048, kChunkBytes, 1024);
-            ptx::mma_pair_f16(tmem + kColO + 128 * nh, a, bd, kIdesc,
+          for (int kk = 0; kk < 4; ++kk)
+            ptx::mma_pair_f16(tmem + kColO + 128 * nh, ptx::make_desc(pa + kk * 2, kHi),
+                              ptx::make_desc(vb + kk * 128, kHi), kIdesc,
                               (first && th == 0 && kk == 0 && part == 0) ? 0u : 1u);
-          }
         }
         ptx::mma_commit_pair_mc(vempty0 + 8 * ring.stage, 0x3);
         ring.advance();
       }
-      ptx::mma_commit_pair_mc(o_done, 0x3);
+      ptx::mma_commit_pair_mc(o_done0 + 8 * b, 0x3);
     }
     ++piece;
   }
@@ -409,6 +492,44 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Workspace slot of sequence bb's piece inside pair pp's range.
+__device__ __forceinline__ size_t pair_slot(int pp, int bb, long long total_tiles, int pairs, int nt,
+                                            int maxp) {
+  return (size_t)pp * maxp + (bb - (int)((long long)pp * total_tiles / pairs / nt));
+}
+
+// First and last pair whose tile range [p*T/P, (p+1)*T/P) meets sequence bb.
+__device__ __forceinline__ void pairs_of_sequence(long long total_tiles, int pairs, int nt, int bb,
+                                                  int* pf, int* pl) {
+  const long long x0 = (long long)bb * nt;
+  *pf = (int)(((x0 + 1) * pairs + total_tiles - 1) / total_tiles) - 1;
+  *pl = (int)(((x0 + nt) * pairs + total_tiles - 1) / total_tiles) - 1;
+}
+
+// Q latent dims [0, 256) of sequence `bb` into TMEM (A operand of the first 16
+// QK^T k-steps): lane L <- row L % 64 of this CTA's heads, so both lane halves
+// hold the rows (the duplicated layout of a pair MMA's A operand in TMEM).
+__device__ __forceinline__ void write_qt(const Params& p, int bb, uint32_t rank, int m, uint32_t tmem,
+                                         uint32_t lane_off) {
+  const uint4* src =
+      reinterpret_cast<const uint4*>(p.q + ((size_t)bb * kHeads + 64 * rank + m) * (kDim * 2));
+  // all 32 loads in flight at once (one memory round trip), then four TMEM stores
+  uint32_t w[4][32];
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      const uint4 x = __ldg(src + 8 * cc + g);
+      w[cc][4 * g] = x.x;
+      w[cc][4 * g + 1] = x.y;
+      w[cc][4 * g + 2] = x.z;
+      w[cc][4 * g + 3] = x.w;
+    }
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc) ptx::tmem_st32(tmem + lane_off + kColQT + 32 * cc, w[cc]);
+  ptx::tmem_wait_st();
+}
+
 template <typename T>
 __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, uint32_t rank, int pair,
                                                  uint8_t* smem, uint32_t tmem, Barriers* bars, int wq,
@@ -422,10 +543,18 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
   float* xl = reinterpret_cast<float*>(smem + S::kXl);
   const uint32_t s_full0 = ptx::smem_u32(&bars->s_full[0]);
   const uint32_t xchg0 = ptx::smem_u32(&bars->xchg[0]);
-  const uint32_t o_done = ptx::smem_u32(&bars->o_done);
+  const uint32_t o_done0 = ptx::smem_u32(&bars->o_done[0]);
   const uint32_t lx = ptx::smem_u32(&bars->lx);
+  const uint32_t mg = ptx::smem_u32(&bars->mg);
+  const uint32_t mg2 = ptx::smem_u32(&bars->mg2);
+  volatile uint32_t* merge_flag = reinterpret_cast<volatile uint32_t*>(smem + S::kMisc + 8);
+  uint32_t nsplit = 0;   // split pieces finished by this CTA (merge handshake phase)
+  uint32_t nstage = 0, ndone = 0;   // merge staging rounds (barrier phases)
+  const uint32_t mload = ptx::smem_u32(&bars->mload);
+  const uint32_t mdone = ptx::smem_u32(&bars->mdone);
+  const uint32_t qt_full_leader = ptx::mapa(ptx::smem_u32(&bars->qt_full), 0);
   const uint32_t s_free0_leader = ptx::mapa(ptx::smem_u32(&bars->s_free[0]), 0);
-  const uint32_t p_full_leader = ptx::mapa(ptx::smem_u32(&bars->p_full), 0);
+  const uint32_t p_full0_leader = ptx::mapa(ptx::smem_u32(&bars->p_full[0]), 0);
   const uint32_t o_free_leader = ptx::mapa(ptx::smem_u32(&bars->o_free), 0);
   const float sl2 = p.sl2;
   uint32_t gi = 0;
@@ -433,7 +562,17 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
   PieceIter it(p, pair);
   Piece pc;
   int piece = 0;
-  while (it.next(&pc)) {
+  bool have = it.next(&pc);
+  if (have) {
+    write_qt(p, pc.bb, rank, m, tmem, lane_off);
+    ptx::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive_cluster(qt_full_leader);
+  }
+  while (have) {
+    PieceIter peek = it;
+    Piece nxt;
+    const bool has_next = peek.next(&nxt);
     float m_run = -INFINITY, l = 0.f;
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j, ++gi) {
@@ -448,6 +587,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(s_free0_leader + 8 * b);
+
       float v[64];
 #pragma unroll
       for (int k = 0; k < 32; ++k) {
@@ -460,13 +600,17 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         for (int k = 0; k < 64; ++k)
           if (k >= nvalid) v[k] = -INFINITY;
       }
-      float mx = v[0];
+      float mx8[8];
 #pragma unroll
-      for (int k = 1; k < 64; ++k) mx = fmaxf(mx, v[k]);
+      for (int k = 0; k < 8; ++k) mx8[k] = v[k];
+#pragma unroll
+      for (int k = 8; k < 64; ++k) mx8[k & 7] = fmaxf(mx8[k & 7], v[k]);
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       // the two lane halves of a row hold its two 64-token halves: exchange maxima
       xmax[b * 128 + L] = mx;
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(xchg0 + 8 * b, rank));
+      if (lane == 0) ptx::mbar_arrive_local(xchg0 + 8 * b);
       if (!wait_bar(c, xchg0 + 8 * b, (gi >> 1) & 1u, kErrSoftmax)) return;
       mx = fmaxf(mx, xmax[b * 128 + (L ^ 64)]);
       const float m_new = fmaxf(m_run, mx);
@@ -493,11 +637,13 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         }
       }
       l += ls;
-      if (j > pc.first) {
-        // P.V of the previous tile must be complete before O is touched or P rewritten
-        if (!wait_bar(c, o_done, (gi - 1) & 1u, kErrSoftmax)) return;
+      // P buffer b was last read by P.V of tile gi - 2
+      if (gi >= 2 && !wait_bar(c, o_done0 + 8 * b, ((gi - 2) >> 1) & 1u, kErrSoftmax)) return;
+      if (j > pc.first && __any_sync(0xffffffffu, rescale)) {
+        // rare: O must be rescaled, after P.V of the previous tile has landed in it
+        if (!wait_bar(c, o_done0 + 8 * (b ^ 1u), ((gi - 1) >> 1) & 1u, kErrSoftmax)) return;
         ptx::tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
+        {
 #pragma unroll 1
           for (int cc = 0; cc < 8; ++cc) {
             uint32_t o[32];
@@ -511,7 +657,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         }
       }
       // P row m of token half hf, SWIZZLE_128B: 16-byte granule g at g ^ (m & 7)
-      uint8_t* prow = smem + S::kP + hf * kChunkBytes + m * 128;
+      uint8_t* prow = smem + S::kP + b * S::kPBuf + hf * kChunkBytes + m * 128;
 #pragma unroll
       for (int g = 0; g < 8; ++g) {
         const uint32_t off = (uint32_t)((g ^ (m & 7)) << 4);
@@ -524,15 +670,22 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
       ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive_cluster(p_full_leader);
+      if (lane == 0) ptx::mbar_arrive_cluster(p_full0_leader + 8 * b);
+      if (j == pc.end - 1 && has_next) {
+        // this piece's QK^T is complete (its last S was read): the next piece's Q goes to TMEM
+        write_qt(p, nxt.bb, rank, m, tmem, lane_off);
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive_cluster(qt_full_leader);
+      }
     }
 
-    // ---- epilogue of this piece
-    if (!wait_bar(c, o_done, (gi - 1) & 1u, kErrSoftmax)) return;
+    // ---- epilogue of this piece: wait for P.V of its last tile
+    if (!wait_bar(c, o_done0 + 8 * ((gi - 1) & 1u), ((gi - 1) >> 1) & 1u, kErrSoftmax)) return;
     ptx::tc_fence_after();
     xl[L] = l;
     __syncwarp();
-    if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(lx, rank));
+    if (lane == 0) ptx::mbar_arrive_local(lx);
     if (!wait_bar(c, lx, (uint32_t)piece & 1u, kErrSoftmax)) return;
     const float ltot = l + xl[L ^ 64];
     const float inv = 1.f / ltot;
@@ -575,10 +728,148 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         p.part_lse[(size_t)slot * kHeads + head] = lse;
       }
     }
+    if (!pc.full) {
+      // The sequence was split across pairs.  Publish this piece, count it, and if
+      // it completes the sequence's set, merge all pieces into `out` (the LSE
+      // combine of mla_decode.py:212-246, fused: no second launch, no waiting on
+      // other CTAs -- the last one to finish does the merge).
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive_local(mg);
+      if (!wait_bar(c, mg, nsplit & 1u, kErrSoftmax)) return;
+      int pf, pl;
+      pairs_of_sequence(p.total_tiles, p.pairs, p.nt, pc.bb, &pf, &pl);
+      if (L == 0) {
+        uint32_t* cnt = p.counters + 2 * pc.bb + rank;
+        const uint32_t done = atomicAdd(cnt, 1u) + 1u;
+        const bool last = done == (uint32_t)(pl - pf + 1);
+        if (last) atomicExch(cnt, 0u);   // ready for the next call
+        *merge_flag = last ? 1u : 0u;
+        ptx::mbar_arrive_local(mg2);
+      }
+      if (!wait_bar(c, mg2, nsplit & 1u, kErrSoftmax)) return;
+      const bool last = *merge_flag != 0u;
+      ++nsplit;
+      if (last) {
+        __threadfence();
+        const int own = pair;
+        float mx = lse;
+        for (int pp = pf; pp <= pl; ++pp)
+          if (pp != own)
+            mx = fmaxf(mx, __ldcg(p.part_lse + pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp) *
+                                                  kHeads + head));
+        float sum = exp2f((lse - mx) * kLog2e);
+        for (int pp = pf; pp <= pl; ++pp)
+          if (pp != own)
+            sum += exp2f((__ldcg(p.part_lse + pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp) *
+                                                   kHeads + head) - mx) * kLog2e);
+        const float big = mx + logf(sum);
+        T* orow = static_cast<T*>(p.out) + ((size_t)pc.bb * kHeads + head) * kDim;
+        if (!has_next) {
+          // Last piece of this pair: the rings and Q/P buffers are idle.  O (this
+          // piece, unnormalised) is still in TMEM: scale it by its merge weight,
+          // then add each other piece, staged row by row into shared memory.
+          const float w_own = exp2f((lse - big) * kLog2e) * inv;
+#pragma unroll 1
+          for (int cc = 0; cc < 8; ++cc) {
+            uint32_t o[32];
+            ptx::tmem_ld32(tmem + lane_off + kColO + 32 * cc, o);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * w_own);
+            ptx::tmem_st32(tmem + lane_off + kColO + 32 * cc, o);
+          }
+          ptx::tmem_wait_st();
+          const uint32_t stage = ptx::smem_u32(smem);
+          for (int pp = pf; pp <= pl; ++pp) {
+            if (pp == own) continue;
+            const size_t sl = pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp);
+            const float w = exp2f((__ldcg(p.part_lse + sl * kHeads + head) - big) * kLog2e);
+            if (L == 0) {
+              ptx::mbar_arrive_expect_tx(mload, 64 * kDim * 4);
+              const float* src = p.part_o + (sl * kHeads + 64 * rank) * kDim;
+              for (int r = 0; r < 64; ++r)
+                ptx::bulk_load(stage + r * kMergePitch, src + (size_t)r * kDim, kDim * 4, mload);
+            }
+            if (!wait_bar(c, mload, nstage & 1u, kErrSoftmax)) return;
+            ++nstage;
+            const float* srow = reinterpret_cast<const float*>(smem + m * kMergePitch);
+#pragma unroll 1
+            for (int cc = 0; cc < 8; ++cc) {
+              const int d0 = 256 * (cc >> 2) + 128 * hf + 32 * (cc & 3);
+              uint32_t o[32];
+              ptx::tmem_ld32(tmem + lane_off + kColO + 32 * cc, o);
+              ptx::tmem_wait_ld();
+#pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                const float4 x = *reinterpret_cast<const float4*>(srow + d0 + 4 * g);
+                o[4 * g] = __float_as_uint(fmaf(w, x.x, __uint_as_float(o[4 * g])));
+                o[4 * g + 1] = __float_as_uint(fmaf(w, x.y, __uint_as_float(o[4 * g + 1])));
+                o[4 * g + 2] = __float_as_uint(fmaf(w, x.z, __uint_as_float(o[4 * g + 2])));
+                o[4 * g + 3] = __float_as_uint(fmaf(w, x.w, __uint_as_float(o[4 * g + 3])));
+              }
+              ptx::tmem_st32(tmem + lane_off + kColO + 32 * cc, o);
+            }
+            ptx::tmem_wait_st();
+            // everyone is done reading the stage before it is refilled
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive_local(mdone);
+            if (!wait_bar(c, mdone, ndone & 1u, kErrSoftmax)) return;
+            ++ndone;
+          }
+#pragma unroll 1
+          for (int cc = 0; cc < 8; ++cc) {
+            uint32_t o[32];
+            ptx::tmem_ld32(tmem + lane_off + kColO + 32 * cc, o);
+            ptx::tmem_wait_ld();
+            T* dst = orow + 256 * (cc >> 2) + 128 * hf + 32 * (cc & 3);
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+              reinterpret_cast<uint4*>(dst)[g] = make_uint4(
+                  pack2<T>(__uint_as_float(o[8 * g]), __uint_as_float(o[8 * g + 1])),
+                  pack2<T>(__uint_as_float(o[8 * g + 2]), __uint_as_float(o[8 * g + 3])),
+                  pack2<T>(__uint_as_float(o[8 * g + 4]), __uint_as_float(o[8 * g + 5])),
+                  pack2<T>(__uint_as_float(o[8 * g + 6]), __uint_as_float(o[8 * g + 7])));
+          }
+        } else {
+          // rare (a sequence split over three or more pairs): merge from global memory
+#pragma unroll 1
+          for (int cc = 0; cc < 8; ++cc) {
+            const int d0 = 256 * (cc >> 2) + 128 * hf + 32 * (cc & 3);
+            float acc[32];
+#pragma unroll
+            for (int k = 0; k < 32; ++k) acc[k] = 0.f;
+            for (int pp = pf; pp <= pl; ++pp) {
+              const size_t sl = pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp);
+              const float w = exp2f((__ldcg(p.part_lse + sl * kHeads + head) - big) * kLog2e);
+              const float4* src = reinterpret_cast<const float4*>(p.part_o + (sl * kHeads + head) * kDim + d0);
+#pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                const float4 x = __ldcg(src + g);
+                acc[4 * g] = fmaf(w, x.x, acc[4 * g]);
+                acc[4 * g + 1] = fmaf(w, x.y, acc[4 * g + 1]);
+                acc[4 * g + 2] = fmaf(w, x.z, acc[4 * g + 2]);
+                acc[4 * g + 3] = fmaf(w, x.w, acc[4 * g + 3]);
+              }
+            }
+            T* dst = orow + d0;
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+              reinterpret_cast<uint4*>(dst)[g] =
+                  make_uint4(pack2<T>(acc[8 * g], acc[8 * g + 1]), pack2<T>(acc[8 * g + 2], acc[8 * g + 3]),
+                             pack2<T>(acc[8 * g + 4], acc[8 * g + 5]), pack2<T>(acc[8 * g + 6], acc[8 * g + 7]));
+          }
+        }
+        if (hf == 0 && p.lse_out != nullptr) p.lse_out[(size_t)pc.bb * kHeads + head] = big;
+      }
+    }
     ptx::tc_fence_before();
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive_cluster(o_free_leader);
     ++piece;
+    it = peek;
+    pc = nxt;
+    have = has_next;
   }
 }
 
@@ -610,15 +901,22 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
     }
     ptx::mbar_init(ptx::smem_u32(&bars->q_full), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->q_empty), 1);
+    ptx::mbar_init(ptx::smem_u32(&bars->qt_full), 8);
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(ptx::smem_u32(&bars->s_full[b]), 1);
       ptx::mbar_init(ptx::smem_u32(&bars->s_free[b]), 8);
       ptx::mbar_init(ptx::smem_u32(&bars->xchg[b]), 4);
     }
-    ptx::mbar_init(ptx::smem_u32(&bars->p_full), 8);
-    ptx::mbar_init(ptx::smem_u32(&bars->o_done), 1);
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(ptx::smem_u32(&bars->p_full[b]), 8);
+      ptx::mbar_init(ptx::smem_u32(&bars->o_done[b]), 1);
+    }
     ptx::mbar_init(ptx::smem_u32(&bars->o_free), 8);
     ptx::mbar_init(ptx::smem_u32(&bars->lx), 4);
+    ptx::mbar_init(ptx::smem_u32(&bars->mg), 4);
+    ptx::mbar_init(ptx::smem_u32(&bars->mg2), 1);
+    ptx::mbar_init(ptx::smem_u32(&bars->mload), 1);
+    ptx::mbar_init(ptx::smem_u32(&bars->mdone), 4);
     ptx::mbar_init(ptx::smem_u32(&bars->drain_qk), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->drain_pv), 1);
     *abort_flag = 0u;
@@ -643,6 +941,7 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
 
   if (warp == 0) {
     if (lane == 0) k_producer<T>(p, c, rank, pair, sbase, bars);
+    else if (lane == 16) q_loader<T>(p, c, rank, pair, sbase, bars);
   } else if (warp == 1) {
     if (rank == 0 && lane == 0) {
       qk_issuer<T>(p, c, pair, sbase, tmem, bars);
@@ -682,56 +981,76 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
 // sequences that one pair covered whole were written directly and are skipped.
 // Same LSE algebra as mla_combine.cu (mla_decode.py:212-246).
 // ---------------------------------------------------------------------------
-constexpr int kMaxPairs = 256;
+constexpr int kMaxPairs = 256;   // pairs per launch (schedule bound)
 
 template <typename T>
 __global__ void __launch_bounds__(128)
 mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__ part_o,
                         T* __restrict__ out, float* __restrict__ lse_out, long long total_tiles,
                         int nt, int pairs, int maxp) {
-  __shared__ float s_w[kMaxPairs];
-  __shared__ int s_slot[kMaxPairs];
-  __shared__ float s_lse;
   const int head = blockIdx.x, bb = blockIdx.y, tid = threadIdx.x;
   const long long x0 = (long long)bb * nt;
-  // first/last pair whose range [p*T/P, (p+1)*T/P) meets this sequence's tiles
-  const int pf = (int)(((x0 + 1) * pairs + total_tiles - 1) / total_tiles) - 1;
-  const int pl = (int)(((x0 + nt) * pairs + total_tiles - 1) / total_tiles) - 1;
-  if (pf == pl) return;
+  (void)x0;
+  int pf, pl;
+  pairs_of_sequence(total_tiles, pairs, nt, bb, &pf, &pl);
+  if (pf == pl) return;   // one pair covered the whole sequence and wrote `out` itself
   const int n = pl - pf + 1;
-  if (tid == 0) {
-    float mx = -INFINITY;
-    for (int k = 0; k < n; ++k) {
-      const int pp = pf + k;
-      const long long t0 = (long long)pp * total_tiles / pairs;
-      const int slot = pp * maxp + (bb - (int)(t0 / nt));
-      s_slot[k] = slot;
-      s_w[k] = part_lse[(size_t)slot * kHeads + head];
-      mx = fmaxf(mx, s_w[k]);
-    }
-    float sum = 0.f;
-    for (int k = 0; k < n; ++k) sum += exp2f((s_w[k] - mx) * kLog2e);
-    const float lse = mx + logf(sum);
-    for (int k = 0; k < n; ++k) s_w[k] = exp2f((s_w[k] - lse) * kLog2e);
-    s_lse = lse;
-  }
-  __syncthreads();
+  // Every thread loads the (few) split LSEs itself -- broadcast loads, issued together --
+  // and its 4 columns of every partial row, then merges; no serial thread-0 phase.
+  constexpr int kFast = 8;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 1
-  for (int k = 0; k < n; ++k) {
-    const float4 v = __ldg(
-        reinterpret_cast<const float4*>(part_o + ((size_t)s_slot[k] * kHeads + head) * kDim) + tid);
-    const float w = s_w[k];
-    acc.x = fmaf(w, v.x, acc.x);
-    acc.y = fmaf(w, v.y, acc.y);
-    acc.z = fmaf(w, v.z, acc.z);
-    acc.w = fmaf(w, v.w, acc.w);
+  float lse;
+  if (n <= kFast) {
+    float lk[kFast];
+    float4 vk[kFast];
+#pragma unroll
+    for (int k = 0; k < kFast; ++k) {
+      if (k < n) {
+        const size_t sl = pair_slot(pf + k, bb, total_tiles, pairs, nt, maxp);
+        lk[k] = __ldg(part_lse + sl * kHeads + head);
+        vk[k] = __ldg(reinterpret_cast<const float4*>(part_o + (sl * kHeads + head) * kDim) + tid);
+      } else {
+        lk[k] = -INFINITY;
+        vk[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float mx = lk[0];
+#pragma unroll
+    for (int k = 1; k < kFast; ++k) mx = fmaxf(mx, lk[k]);
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < kFast; ++k) sum += exp2f((lk[k] - mx) * kLog2e);
+    lse = mx + logf(sum);
+#pragma unroll
+    for (int k = 0; k < kFast; ++k) {
+      const float w = exp2f((lk[k] - lse) * kLog2e);
+      acc.x = fmaf(w, vk[k].x, acc.x);
+      acc.y = fmaf(w, vk[k].y, acc.y);
+      acc.z = fmaf(w, vk[k].z, acc.z);
+      acc.w = fmaf(w, vk[k].w, acc.w);
+    }
+  } else {
+    float mx = -INFINITY;
+    for (int k = 0; k < n; ++k) mx = fmaxf(mx, __ldg(part_lse + pair_slot(pf + k, bb, total_tiles, pairs, nt, maxp) * kHeads + head));
+    float sum = 0.f;
+    for (int k = 0; k < n; ++k)
+      sum += exp2f((__ldg(part_lse + pair_slot(pf + k, bb, total_tiles, pairs, nt, maxp) * kHeads + head) - mx) * kLog2e);
+    lse = mx + logf(sum);
+    for (int k = 0; k < n; ++k) {
+      const size_t sl = pair_slot(pf + k, bb, total_tiles, pairs, nt, maxp);
+      const float w = exp2f((__ldg(part_lse + sl * kHeads + head) - lse) * kLog2e);
+      const float4 v = __ldg(reinterpret_cast<const float4*>(part_o + (sl * kHeads + head) * kDim) + tid);
+      acc.x = fmaf(w, v.x, acc.x);
+      acc.y = fmaf(w, v.y, acc.y);
+      acc.z = fmaf(w, v.z, acc.z);
+      acc.w = fmaf(w, v.w, acc.w);
+    }
   }
   uint2 o;
   o.x = pack2<T>(acc.x, acc.y);
   o.y = pack2<T>(acc.z, acc.w);
   reinterpret_cast<uint2*>(out + ((size_t)bb * kHeads + head) * kDim)[tid] = o;
-  if (lse_out != nullptr && tid == 0) lse_out[(size_t)bb * kHeads + head] = s_lse;
+  if (lse_out != nullptr && tid == 0) lse_out[(size_t)bb * kHeads + head] = lse;
 }
 
 // ---------------------------------------------------------------------------
@@ -867,11 +1186,16 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int) {
   if (!make_map(&p.tm_kv, a.kv, kDim, kv_rows, dt) || !make_map(&p.tm_kpe, a.k_pe, kPeDim, kv_rows, dt) ||
       !make_map(&p.tm_q, a.q, kDim, q_rows, dt) || !make_map(&p.tm_qpe, a.q_pe, kPeDim, q_rows, dt))
     return cudaErrorInvalidValue;
+  p.kv = static_cast<const uint8_t*>(a.kv);
+  p.q = static_cast<const uint8_t*>(a.q);
+  p.qpe = static_cast<const uint8_t*>(a.q_pe);
+  p.kpe = static_cast<const uint8_t*>(a.k_pe);
   p.out = a.out;
   p.lse_out = a.lse;
   p.part_o = a.part_o;
   p.part_lse = a.part_lse;
   p.status = a.status;
+  p.counters = a.counters;
   p.batch = a.batch;
   p.seqlen = a.seqlen_kv;
   p.nt = (a.seqlen_kv + kTile - 1) / kTile;

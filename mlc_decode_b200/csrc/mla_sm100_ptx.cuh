@@ -42,7 +42,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
@@ -57,8 +57,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 }
 // Arrive (count 1) on a barrier given by a shared::cluster address (any CTA of the cluster).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// Arrive (count 1) on a barrier of this CTA.
+__device__ __forceinline__ void mbar_arrive_local(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 // ---------------------------------------------------------------- cluster
@@ -80,6 +83,23 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst_smem, const void* 
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst_smem),
       "l"(reinterpret_cast<uint64_t>(desc)), "r"(cluster_bar), "r"(x), "r"(y)
       : "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from global memory
+// into this CTA's shared memory, completion counted on the local barrier `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_smem),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// Prefetch `bytes` (multiple of 16) of global memory at `src` into L2.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),
+               "r"(bytes)
+               : "memory");
 }
 
 // ---------------------------------------------------------------- proxies
@@ -114,6 +134,16 @@ __device__ __forceinline__ void mma_pair_f16(uint32_t d_tmem, uint64_t a_desc, u
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem] (A in the duplicated 2x64-lane layout of the pair MMA).
+__device__ __forceinline__ void mma_pair_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // Arrive once on the barrier at offset `bar` of every CTA in `cta_mask` when all
@@ -159,18 +189,25 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 }
 
 // ---------------------------------------------------------------- descriptors
-// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1.
-// lbo/sbo in bytes.  K-major operands: sbo = stride between 8-row groups, lbo
-// unused (1).  MN-major operands: lbo = stride between 64-element MN atoms,
-// sbo = stride between 8-row K groups.
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1,
+// as two 32-bit words.  The low word holds the start address (bits 0-13, in
+// 16-byte units) and the leading byte offset (bits 16-29); the high word the
+// stride byte offset (bits 32-45), the version (bit 46) and the layout (61-63).
+// K-major operands: sbo = stride between 8-row groups, lbo unused (16).
+// MN-major operands: lbo = stride between 64-element MN atoms, sbo = stride
+// between 8-row K groups.  Offsets inside a descriptor's reach are added to the
+// low word in 16-byte units (addresses stay below 256 KB, no carry).
+__host__ __device__ constexpr uint32_t sw128_desc_hi(uint32_t sbo) {
+  return ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+}
+__device__ __forceinline__ uint32_t sw128_desc_lo(uint32_t smem_addr, uint32_t lbo) {
+  return ((smem_addr >> 4) & 0x3FFFu) | (((lbo >> 4) & 0x3FFFu) << 16);
+}
+__device__ __forceinline__ uint64_t make_desc(uint32_t lo, uint32_t hi) {
+  return (static_cast<uint64_t>(hi) << 32) | lo;
+}
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-  d |= (uint64_t)1u << 46;   // descriptor version (sm_100)
-  d |= (uint64_t)2u << 61;   // SWIZZLE_128B
-  return d;
+  return make_desc(sw128_desc_lo(smem_addr, lbo), sw128_desc_hi(sbo));
 }
 
 // Instruction descriptor of kind::f16 with f32 accumulation.

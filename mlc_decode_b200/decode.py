@@ -135,9 +135,13 @@ class MlaDecodeKernel:
             return 0
         return int(ws[:4].view(torch.int32).item())
 
+    def plan(self, dtype=torch.bfloat16) -> dict:
+        """The library's plan for this shape: kernel, splits/pairs, launches per call."""
+        return capi.describe_plan(self.batch, self.heads, self.seqlen_kv, _DTYPES[dtype], self._ccfg)
+
     def launches_per_call(self, dtype=torch.bfloat16) -> int:
-        """Kernels one call enqueues (1 for a single-split plan, else 2)."""
-        return 2 if self.workspace_bytes(dtype) > 0 else 1
+        """Kernels one call enqueues."""
+        return self.plan(dtype)["launches"]
 
     def get_kernel_source(self) -> str:
         """CUDA source of the kernels this object launches (cf. dump_kernel_src.py:40)."""
