@@ -102,7 +102,8 @@ struct Barriers {
   uint64_t s_full[2], s_free[2];
   uint64_t p_full[2];
   uint64_t xchg[2];
-  uint64_t o_done[2], o_free, lx, mg, mg2, mload, mdone;
+  uint64_t o_done[2], o_free, lx, stg, stg2, mload, mdone;
+  uint64_t qts, qtr;     // Q dims [0, 256) staged in shared memory / copied to TMEM
   uint64_t drain_qk, drain_pv;
 };
 static_assert(sizeof(Barriers) <= 512, "barrier block");
@@ -128,9 +129,11 @@ struct Params {
   CUtensorMap tm_kpe;   // [b*s, 64]
   CUtensorMap tm_q;     // [b*128, 512]
   CUtensorMap tm_qpe;   // [b*128, 64]
+  CUtensorMap tm_out;   // [b*128, 512] output rows, box 64 x 64 (stores)
+  CUtensorMap tm_part;  // [slots*128, 512] float32 partial rows, box 32 x 64 (stores)
   const uint8_t* kv;    // raw rows, for L2 prefetch
   const uint8_t* kpe;
-  const uint8_t* q;     // raw Q rows, for the TMEM copy of dims [0, 256)
+  const uint8_t* q;     // raw Q rows, for L2 prefetch
   const uint8_t* qpe;
   void* out;
   float* lse_out;
@@ -285,9 +288,11 @@ __device__ __forceinline__ void prefetch_q(const Params& p, int bb, uint32_t ran
 }
 
 // ---------------------------------------------------------------------------
-// Q loader: per piece, Q dims [256, 512) and the rope dims into shared memory
-// once the previous piece's QK^T no longer reads them; the next piece's rows
-// are pulled into L2 ahead of time (they also feed the TMEM copy).
+// Q loader, per piece, once the previous piece's QK^T no longer reads the Q
+// region: first Q dims [0, 256) of this CTA's rows (staged for the softmax
+// warps, which copy them into TMEM), then, once copied, Q dims [256, 512) and
+// the rope dims for the shared-memory operand.  The next piece's rows are
+// pulled into L2 ahead of time.
 // ---------------------------------------------------------------------------
 template <typename T>
 __device__ __forceinline__ void q_loader(const Params& p, const Ctx& c, uint32_t rank, int pair,
@@ -297,6 +302,8 @@ __device__ __forceinline__ void q_loader(const Params& p, const Ctx& c, uint32_t
   const uint32_t q_full = ptx::smem_u32(&bars->q_full);
   const uint32_t q_full_leader = ptx::mapa(q_full, 0);
   const uint32_t q_empty = ptx::smem_u32(&bars->q_empty);
+  const uint32_t qts = ptx::smem_u32(&bars->qts);
+  const uint32_t qtr = ptx::smem_u32(&bars->qtr);
   PieceIter it(p, pair);
   {
     PieceIter first = it;
@@ -310,8 +317,13 @@ __device__ __forceinline__ void q_loader(const Params& p, const Ctx& c, uint32_t
     Piece nxt;
     if (peek.next(&nxt)) prefetch_q(p, nxt.bb, rank);
     if (piece > 0 && !wait_bar(c, q_empty, (uint32_t)(piece - 1) & 1u, kErrKLoad)) return;
-    if (leader) ptx::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
     const int qrow = pc.bb * kHeads + 64 * (int)rank;
+    ptx::mbar_arrive_expect_tx(qts, 4 * kChunkBytes);
+#pragma unroll 1
+    for (int ch = 0; ch < 4; ++ch)
+      ptx::tma_load_2d_local(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, qts, 64 * ch, qrow);
+    if (!wait_bar(c, qtr, (uint32_t)piece & 1u, kErrKLoad)) return;
+    if (leader) ptx::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
 #pragma unroll 1
     for (int ch = 0; ch < 4; ++ch)
       ptx::tma_load_2d_pair(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, q_full_leader, kQTDims + 64 * ch,
@@ -506,28 +518,36 @@ __device__ __forceinline__ void pairs_of_sequence(long long total_tiles, int pai
   *pl = (int)(((x0 + nt) * pairs + total_tiles - 1) / total_tiles) - 1;
 }
 
-// Q latent dims [0, 256) of sequence `bb` into TMEM (A operand of the first 16
-// QK^T k-steps): lane L <- row L % 64 of this CTA's heads, so both lane halves
-// hold the rows (the duplicated layout of a pair MMA's A operand in TMEM).
-__device__ __forceinline__ void write_qt(const Params& p, int bb, uint32_t rank, int m, uint32_t tmem,
-                                         uint32_t lane_off) {
-  const uint4* src =
-      reinterpret_cast<const uint4*>(p.q + ((size_t)bb * kHeads + 64 * rank + m) * (kDim * 2));
-  // all 32 loads in flight at once (one memory round trip), then four TMEM stores
-  uint32_t w[4][32];
+// Copy this CTA's staged Q rows, latent dims [0, 256) (four SW128 boxes at the
+// start of the Q region), into TMEM as the A operand of the first 16 QK^T
+// k-steps: lane L <- row L % 64, so both lane halves hold the rows (the
+// duplicated layout of a pair MMA's A operand in TMEM).
+template <typename T>
+__device__ __forceinline__ void copy_qt(const uint8_t* smem, int m, uint32_t tmem, uint32_t lane_off) {
+  using S = Smem<T>;
 #pragma unroll
-  for (int cc = 0; cc < 4; ++cc)
+  for (int ch = 0; ch < 4; ++ch) {
+    const uint8_t* row = smem + S::kQ + ch * kChunkBytes + m * 128;
+    uint32_t w[32];
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
-      const uint4 x = __ldg(src + 8 * cc + g);
-      w[cc][4 * g] = x.x;
-      w[cc][4 * g + 1] = x.y;
-      w[cc][4 * g + 2] = x.z;
-      w[cc][4 * g + 3] = x.w;
+      const uint4 x = *reinterpret_cast<const uint4*>(row + ((g ^ (m & 7)) << 4));
+      w[4 * g] = x.x;
+      w[4 * g + 1] = x.y;
+      w[4 * g + 2] = x.z;
+      w[4 * g + 3] = x.w;
     }
-#pragma unroll
-  for (int cc = 0; cc < 4; ++cc) ptx::tmem_st32(tmem + lane_off + kColQT + 32 * cc, w[cc]);
+    ptx::tmem_st32(tmem + lane_off + kColQT + 32 * ch, w);
+  }
   ptx::tmem_wait_st();
+}
+
+// Row m (128 bytes) of an SW128 staging box: 16-byte granule g at g ^ (m & 7).
+__device__ __forceinline__ void st_box_row(uint8_t* box, int m, const uint32_t (&w)[32]) {
+#pragma unroll
+  for (int g = 0; g < 8; ++g)
+    *reinterpret_cast<uint4*>(box + m * 128 + ((g ^ (m & 7)) << 4)) =
+        make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
 }
 
 template <typename T>
@@ -541,15 +561,21 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
   const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
   float* xmax = reinterpret_cast<float*>(smem + S::kXmax);
   float* xl = reinterpret_cast<float*>(smem + S::kXl);
+  volatile uint32_t* merge_flag = reinterpret_cast<volatile uint32_t*>(smem + S::kMisc + 8);
+  // epilogue staging: the P buffers, idle between pieces; kSB boxes of 8 KB per
+  // round, kHB of them from each lane half
+  uint8_t* stage = smem + S::kP;
+  constexpr int kSB = 2 * S::kPBuf / kChunkBytes;
+  constexpr int kHB = kSB / 2;
+  const uint32_t stage_u32 = ptx::smem_u32(stage);
   const uint32_t s_full0 = ptx::smem_u32(&bars->s_full[0]);
   const uint32_t xchg0 = ptx::smem_u32(&bars->xchg[0]);
   const uint32_t o_done0 = ptx::smem_u32(&bars->o_done[0]);
   const uint32_t lx = ptx::smem_u32(&bars->lx);
-  const uint32_t mg = ptx::smem_u32(&bars->mg);
-  const uint32_t mg2 = ptx::smem_u32(&bars->mg2);
-  volatile uint32_t* merge_flag = reinterpret_cast<volatile uint32_t*>(smem + S::kMisc + 8);
-  uint32_t nsplit = 0;   // split pieces finished by this CTA (merge handshake phase)
-  uint32_t nstage = 0, ndone = 0;   // merge staging rounds (barrier phases)
+  const uint32_t stg = ptx::smem_u32(&bars->stg);
+  const uint32_t stg2 = ptx::smem_u32(&bars->stg2);
+  const uint32_t qts = ptx::smem_u32(&bars->qts);
+  const uint32_t qtr = ptx::smem_u32(&bars->qtr);
   const uint32_t mload = ptx::smem_u32(&bars->mload);
   const uint32_t mdone = ptx::smem_u32(&bars->mdone);
   const uint32_t qt_full_leader = ptx::mapa(ptx::smem_u32(&bars->qt_full), 0);
@@ -558,17 +584,75 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
   const uint32_t o_free_leader = ptx::mapa(ptx::smem_u32(&bars->o_free), 0);
   const float sl2 = p.sl2;
   uint32_t gi = 0;
+  uint32_t n_lx = 0, n_stg = 0, n_stg2 = 0, n_stage = 0, n_done = 0;   // barrier phases
+
+  // all four softmax warps meet at `bar` (count 4)
+  auto sync4 = [&](uint32_t bar, uint32_t& ph) -> bool {
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive_local(bar);
+    const bool ok = wait_bar(c, bar, ph & 1u, kErrSoftmax);
+    ++ph;
+    return ok;
+  };
+  // thread L == 0 has done something the others must wait for (stg2, count 1)
+  auto wait_leader = [&]() -> bool {
+    if (L == 0) ptx::mbar_arrive_local(stg2);
+    const bool ok = wait_bar(c, stg2, n_stg2 & 1u, kErrSoftmax);
+    ++n_stg2;
+    return ok;
+  };
+  // Q dims [0, 256) of piece `k`, staged by the Q loader, into TMEM
+  auto take_qt = [&](int k) -> bool {
+    if (!wait_bar(c, qts, (uint32_t)k & 1u, kErrSoftmax)) return false;
+    copy_qt<T>(smem, m, tmem, lane_off);
+    ptx::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      ptx::mbar_arrive_local(qtr);
+      ptx::mbar_arrive_cluster(qt_full_leader);
+    }
+    return true;
+  };
+  // stage O (TMEM) x scale as the output rows of this CTA's heads and store them
+  // with TMA; output chunk co = (nh, bx) of a thread is dims 256 nh + 128 hf + 64 bx
+  auto write_out = [&](int bb, float scale) -> bool {
+#pragma unroll 1
+    for (int r = 0; r < 4 / kHB; ++r) {
+#pragma unroll 1
+      for (int i = 0; i < kHB; ++i) {
+        const int co = r * kHB + i;
+        uint32_t a[32], b2[32], w[32];
+        ptx::tmem_ld32(tmem + lane_off + kColO + 64 * co, a);
+        ptx::tmem_ld32(tmem + lane_off + kColO + 64 * co + 32, b2);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          w[k] = pack2<T>(__uint_as_float(a[2 * k]) * scale, __uint_as_float(a[2 * k + 1]) * scale);
+          w[16 + k] = pack2<T>(__uint_as_float(b2[2 * k]) * scale, __uint_as_float(b2[2 * k + 1]) * scale);
+        }
+        st_box_row(stage + (hf * kHB + i) * kChunkBytes, m, w);
+      }
+      ptx::fence_proxy_async_smem();
+      if (!sync4(stg, n_stg)) return false;
+      if (L == 0) {
+        for (int sb = 0; sb < kSB; ++sb) {
+          const int co = r * kHB + sb % kHB;
+          const int x = 256 * (co >> 1) + 128 * (sb / kHB) + 64 * (co & 1);
+          ptx::tma_store_2d(&p.tm_out, stage_u32 + sb * kChunkBytes, x, bb * kHeads + 64 * (int)rank);
+        }
+        ptx::bulk_commit();
+        ptx::bulk_wait_read();
+      }
+      if (!wait_leader()) return false;
+    }
+    return true;
+  };
 
   PieceIter it(p, pair);
   Piece pc;
   int piece = 0;
   bool have = it.next(&pc);
-  if (have) {
-    write_qt(p, pc.bb, rank, m, tmem, lane_off);
-    ptx::tc_fence_before();
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive_cluster(qt_full_leader);
-  }
+  if (have && !take_qt(0)) return;
   while (have) {
     PieceIter peek = it;
     Piece nxt;
@@ -587,7 +671,6 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(s_free0_leader + 8 * b);
-
       float v[64];
 #pragma unroll
       for (int k = 0; k < 32; ++k) {
@@ -643,18 +726,16 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         // rare: O must be rescaled, after P.V of the previous tile has landed in it
         if (!wait_bar(c, o_done0 + 8 * (b ^ 1u), ((gi - 1) >> 1) & 1u, kErrSoftmax)) return;
         ptx::tc_fence_after();
-        {
 #pragma unroll 1
-          for (int cc = 0; cc < 8; ++cc) {
-            uint32_t o[32];
-            ptx::tmem_ld32(tmem + lane_off + kColO + 32 * cc, o);
-            ptx::tmem_wait_ld();
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t o[32];
+          ptx::tmem_ld32(tmem + lane_off + kColO + 32 * cc, o);
+          ptx::tmem_wait_ld();
 #pragma unroll
-            for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-            ptx::tmem_st32(tmem + lane_off + kColO + 32 * cc, o);
-          }
-          ptx::tmem_wait_st();
+          for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+          ptx::tmem_st32(tmem + lane_off + kColO + 32 * cc, o);
         }
+        ptx::tmem_wait_st();
       }
       // P row m of token half hf, SWIZZLE_128B: 16-byte granule g at g ^ (m & 7)
       uint8_t* prow = smem + S::kP + b * S::kPBuf + hf * kChunkBytes + m * 128;
@@ -671,197 +752,186 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(p_full0_leader + 8 * b);
-      if (j == pc.end - 1 && has_next) {
-        // this piece's QK^T is complete (its last S was read): the next piece's Q goes to TMEM
-        write_qt(p, nxt.bb, rank, m, tmem, lane_off);
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive_cluster(qt_full_leader);
-      }
+      // this piece's QK^T is complete (its last S was read): the next piece's Q goes to TMEM
+      if (j == pc.end - 1 && has_next && !take_qt(piece + 1)) return;
     }
 
     // ---- epilogue of this piece: wait for P.V of its last tile
     if (!wait_bar(c, o_done0 + 8 * ((gi - 1) & 1u), ((gi - 1) >> 1) & 1u, kErrSoftmax)) return;
     ptx::tc_fence_after();
+    int pf = 0, pl = 0;
+    if (!pc.full) pairs_of_sequence(p.total_tiles, p.pairs, p.nt, pc.bb, &pf, &pl);
+    uint32_t* cnt = p.counters + 2 * pc.bb + rank;
+    const uint32_t npieces = (uint32_t)(pl - pf + 1);
     xl[L] = l;
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive_local(lx);
-    if (!wait_bar(c, lx, (uint32_t)piece & 1u, kErrSoftmax)) return;
+    // a split sequence whose other pieces are all counted already is completed by this CTA
+    if (!pc.full && L == 0) *merge_flag = (ptx::ld_acquire_gpu(cnt) + 1u == npieces) ? 1u : 0u;
+    if (!sync4(lx, n_lx)) return;
     const float ltot = l + xl[L ^ 64];
     const float inv = 1.f / ltot;
     const float lse = (m_run * sl2 + log2f(ltot)) * kLn2;
     const int head = 64 * (int)rank + m;
-    const int slot = pair * p.maxp + piece;
-#pragma unroll 1
-    for (int nh = 0; nh < 2; ++nh) {
-#pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t o[32];
-        ptx::tmem_ld32(tmem + lane_off + kColO + 128 * nh + 32 * cc, o);
-        ptx::tmem_wait_ld();
-        const int d0 = 256 * nh + 128 * hf + 32 * cc;
-        if (pc.full) {
-          T* dst = static_cast<T*>(p.out) + ((size_t)pc.bb * kHeads + head) * kDim + d0;
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 w;
-            w.x = pack2<T>(__uint_as_float(o[8 * g + 0]) * inv, __uint_as_float(o[8 * g + 1]) * inv);
-            w.y = pack2<T>(__uint_as_float(o[8 * g + 2]) * inv, __uint_as_float(o[8 * g + 3]) * inv);
-            w.z = pack2<T>(__uint_as_float(o[8 * g + 4]) * inv, __uint_as_float(o[8 * g + 5]) * inv);
-            w.w = pack2<T>(__uint_as_float(o[8 * g + 6]) * inv, __uint_as_float(o[8 * g + 7]) * inv);
-            reinterpret_cast<uint4*>(dst)[g] = w;
-          }
-        } else {
-          float* dst = p.part_o + ((size_t)slot * kHeads + head) * kDim + d0;
-#pragma unroll
-          for (int g = 0; g < 8; ++g)
-            reinterpret_cast<float4*>(dst)[g] =
-                make_float4(__uint_as_float(o[4 * g]) * inv, __uint_as_float(o[4 * g + 1]) * inv,
-                            __uint_as_float(o[4 * g + 2]) * inv, __uint_as_float(o[4 * g + 3]) * inv);
-        }
-      }
-    }
-    if (hf == 0) {
-      if (pc.full) {
-        if (p.lse_out != nullptr) p.lse_out[(size_t)pc.bb * kHeads + head] = lse;
-      } else {
-        p.part_lse[(size_t)slot * kHeads + head] = lse;
-      }
-    }
+    bool merge = false;
     if (!pc.full) {
-      // The sequence was split across pairs.  Publish this piece, count it, and if
-      // it completes the sequence's set, merge all pieces into `out` (the LSE
-      // combine of mla_decode.py:212-246, fused: no second launch, no waiting on
-      // other CTAs -- the last one to finish does the merge).
-      __threadfence();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive_local(mg);
-      if (!wait_bar(c, mg, nsplit & 1u, kErrSoftmax)) return;
-      int pf, pl;
-      pairs_of_sequence(p.total_tiles, p.pairs, p.nt, pc.bb, &pf, &pl);
-      if (L == 0) {
-        uint32_t* cnt = p.counters + 2 * pc.bb + rank;
-        const uint32_t done = atomicAdd(cnt, 1u) + 1u;
-        const bool last = done == (uint32_t)(pl - pf + 1);
-        if (last) atomicExch(cnt, 0u);   // ready for the next call
-        *merge_flag = last ? 1u : 0u;
-        ptx::mbar_arrive_local(mg2);
-      }
-      if (!wait_bar(c, mg2, nsplit & 1u, kErrSoftmax)) return;
-      const bool last = *merge_flag != 0u;
-      ++nsplit;
-      if (last) {
+      merge = *merge_flag != 0u;
+      if (!merge) {
+        // Publish this piece (normalised O in fp32 and its LSE) for the CTA that
+        // completes the sequence: the LSE combine of mla_decode.py:212-246, fused
+        // into this kernel (no second launch; nobody waits on another CTA).
+        const int slot = pair * p.maxp + piece;
+        if (hf == 0) p.part_lse[(size_t)slot * kHeads + head] = lse;
+        // fp32 chunk ci = (nh, k) of a thread is dims 256 nh + 128 hf + 32 k
+#pragma unroll 1
+        for (int r = 0; r < 8 / kHB; ++r) {
+#pragma unroll 1
+          for (int i = 0; i < kHB; ++i) {
+            const int ci = r * kHB + i;
+            uint32_t o[32];
+            ptx::tmem_ld32(tmem + lane_off + kColO + 32 * ci, o);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * inv);
+            st_box_row(stage + (hf * kHB + i) * kChunkBytes, m, o);
+          }
+          ptx::fence_proxy_async_smem();
+          if (!sync4(stg, n_stg)) return;
+          if (L == 0) {
+            for (int sb = 0; sb < kSB; ++sb) {
+              const int ci = r * kHB + sb % kHB;
+              const int x = 256 * (ci >> 2) + 128 * (sb / kHB) + 32 * (ci & 3);
+              ptx::tma_store_2d(&p.tm_part, stage_u32 + sb * kChunkBytes, x, slot * kHeads + 64 * (int)rank);
+            }
+            ptx::bulk_commit();
+            ptx::bulk_wait_read();
+          }
+          if (!wait_leader()) return;
+        }
+        // the LSE stores of every thread are ordered before the count below
         __threadfence();
-        const int own = pair;
-        float mx = lse;
-        for (int pp = pf; pp <= pl; ++pp)
-          if (pp != own)
-            mx = fmaxf(mx, __ldcg(p.part_lse + pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp) *
-                                                  kHeads + head));
-        float sum = exp2f((lse - mx) * kLog2e);
-        for (int pp = pf; pp <= pl; ++pp)
-          if (pp != own)
-            sum += exp2f((__ldcg(p.part_lse + pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp) *
-                                                   kHeads + head) - mx) * kLog2e);
-        const float big = mx + logf(sum);
-        T* orow = static_cast<T*>(p.out) + ((size_t)pc.bb * kHeads + head) * kDim;
-        if (!has_next) {
-          // Last piece of this pair: the rings and Q/P buffers are idle.  O (this
-          // piece, unnormalised) is still in TMEM: scale it by its merge weight,
-          // then add each other piece, staged row by row into shared memory.
-          const float w_own = exp2f((lse - big) * kLog2e) * inv;
+        if (!sync4(stg, n_stg)) return;
+        if (L == 0) {
+          ptx::bulk_wait();
+          ptx::fence_proxy_async_all();
+          __threadfence();
+          const uint32_t done = atomicAdd(cnt, 1u) + 1u;
+          const bool last = done == npieces;
+          if (last) atomicExch(cnt, 0u);   // ready for the next call
+          *merge_flag = last ? 1u : 0u;
+        }
+        if (!wait_leader()) return;
+        merge = *merge_flag != 0u;
+      } else if (L == 0) {
+        atomicExch(cnt, 0u);   // every other piece was counted: reset for the next call
+      }
+    }
+    if (!merge) {
+      if (pc.full) {
+        if (!write_out(pc.bb, inv)) return;
+        if (hf == 0 && p.lse_out != nullptr) p.lse_out[(size_t)pc.bb * kHeads + head] = lse;
+      }
+    } else {
+      // this CTA completes a split sequence: merge every piece into `out`
+      __threadfence();
+      const int own = pair;
+      float mx = lse;
+      for (int pp = pf; pp <= pl; ++pp)
+        if (pp != own)
+          mx = fmaxf(mx, __ldcg(p.part_lse + pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp) *
+                                                kHeads + head));
+      float sum = exp2f((lse - mx) * kLog2e);
+      for (int pp = pf; pp <= pl; ++pp)
+        if (pp != own)
+          sum += exp2f((__ldcg(p.part_lse + pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp) *
+                                               kHeads + head) - mx) * kLog2e);
+      const float big = mx + logf(sum);
+      if (!has_next) {
+        // Last piece of this pair: the rings and the Q/P buffers are idle.  O of
+        // this piece is still in TMEM: scale it by its merge weight, then add each
+        // other piece, staged row by row in shared memory (padded rows: threads
+        // reading one column of 32 rows hit distinct banks).
+        const float w_own = exp2f((lse - big) * kLog2e) * inv;
+#pragma unroll 1
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t o[32];
+          ptx::tmem_ld32(tmem + lane_off + kColO + 32 * cc, o);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * w_own);
+          ptx::tmem_st32(tmem + lane_off + kColO + 32 * cc, o);
+        }
+        ptx::tmem_wait_st();
+        const uint32_t mstage = ptx::smem_u32(smem);
+        for (int pp = pf; pp <= pl; ++pp) {
+          if (pp == own) continue;
+          const size_t sl = pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp);
+          const float w = exp2f((__ldcg(p.part_lse + sl * kHeads + head) - big) * kLog2e);
+          if (L == 0) {
+            ptx::fence_proxy_async_all();
+            ptx::mbar_arrive_expect_tx(mload, 64 * kDim * 4);
+            const float* src = p.part_o + (sl * kHeads + 64 * rank) * kDim;
+            for (int r = 0; r < 64; ++r)
+              ptx::bulk_load(mstage + r * kMergePitch, src + (size_t)r * kDim, kDim * 4, mload);
+          }
+          if (!wait_bar(c, mload, n_stage & 1u, kErrSoftmax)) return;
+          ++n_stage;
+          const float* srow = reinterpret_cast<const float*>(smem + m * kMergePitch);
 #pragma unroll 1
           for (int cc = 0; cc < 8; ++cc) {
+            const int d0 = 256 * (cc >> 2) + 128 * hf + 32 * (cc & 3);
             uint32_t o[32];
             ptx::tmem_ld32(tmem + lane_off + kColO + 32 * cc, o);
             ptx::tmem_wait_ld();
 #pragma unroll
-            for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * w_own);
+            for (int g = 0; g < 8; ++g) {
+              const float4 x = *reinterpret_cast<const float4*>(srow + d0 + 4 * g);
+              o[4 * g] = __float_as_uint(fmaf(w, x.x, __uint_as_float(o[4 * g])));
+              o[4 * g + 1] = __float_as_uint(fmaf(w, x.y, __uint_as_float(o[4 * g + 1])));
+              o[4 * g + 2] = __float_as_uint(fmaf(w, x.z, __uint_as_float(o[4 * g + 2])));
+              o[4 * g + 3] = __float_as_uint(fmaf(w, x.w, __uint_as_float(o[4 * g + 3])));
+            }
             ptx::tmem_st32(tmem + lane_off + kColO + 32 * cc, o);
           }
           ptx::tmem_wait_st();
-          const uint32_t stage = ptx::smem_u32(smem);
+          // everyone is done reading the stage before it is refilled or reused
+          if (!sync4(mdone, n_done)) return;
+        }
+        if (!write_out(pc.bb, 1.f)) return;
+      } else {
+        // rare (a sequence split over three or more pairs): merge from global memory
+        T* orow = static_cast<T*>(p.out) + ((size_t)pc.bb * kHeads + head) * kDim;
+#pragma unroll 1
+        for (int cc = 0; cc < 8; ++cc) {
+          const int d0 = 256 * (cc >> 2) + 128 * hf + 32 * (cc & 3);
+          uint32_t o[32];
+          ptx::tmem_ld32(tmem + lane_off + kColO + 32 * cc, o);
+          ptx::tmem_wait_ld();
+          const float w_own = exp2f((lse - big) * kLog2e) * inv;
+          float acc[32];
+#pragma unroll
+          for (int k = 0; k < 32; ++k) acc[k] = __uint_as_float(o[k]) * w_own;
           for (int pp = pf; pp <= pl; ++pp) {
             if (pp == own) continue;
             const size_t sl = pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp);
             const float w = exp2f((__ldcg(p.part_lse + sl * kHeads + head) - big) * kLog2e);
-            if (L == 0) {
-              ptx::mbar_arrive_expect_tx(mload, 64 * kDim * 4);
-              const float* src = p.part_o + (sl * kHeads + 64 * rank) * kDim;
-              for (int r = 0; r < 64; ++r)
-                ptx::bulk_load(stage + r * kMergePitch, src + (size_t)r * kDim, kDim * 4, mload);
+            const float4* src = reinterpret_cast<const float4*>(p.part_o + (sl * kHeads + head) * kDim + d0);
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              const float4 x = __ldcg(src + g);
+              acc[4 * g] = fmaf(w, x.x, acc[4 * g]);
+              acc[4 * g + 1] = fmaf(w, x.y, acc[4 * g + 1]);
+              acc[4 * g + 2] = fmaf(w, x.z, acc[4 * g + 2]);
+              acc[4 * g + 3] = fmaf(w, x.w, acc[4 * g + 3]);
             }
-            if (!wait_bar(c, mload, nstage & 1u, kErrSoftmax)) return;
-            ++nstage;
-            const float* srow = reinterpret_cast<const float*>(smem + m * kMergePitch);
-#pragma unroll 1
-            for (int cc = 0; cc < 8; ++cc) {
-              const int d0 = 256 * (cc >> 2) + 128 * hf + 32 * (cc & 3);
-              uint32_t o[32];
-              ptx::tmem_ld32(tmem + lane_off + kColO + 32 * cc, o);
-              ptx::tmem_wait_ld();
-#pragma unroll
-              for (int g = 0; g < 8; ++g) {
-                const float4 x = *reinterpret_cast<const float4*>(srow + d0 + 4 * g);
-                o[4 * g] = __float_as_uint(fmaf(w, x.x, __uint_as_float(o[4 * g])));
-                o[4 * g + 1] = __float_as_uint(fmaf(w, x.y, __uint_as_float(o[4 * g + 1])));
-                o[4 * g + 2] = __float_as_uint(fmaf(w, x.z, __uint_as_float(o[4 * g + 2])));
-                o[4 * g + 3] = __float_as_uint(fmaf(w, x.w, __uint_as_float(o[4 * g + 3])));
-              }
-              ptx::tmem_st32(tmem + lane_off + kColO + 32 * cc, o);
-            }
-            ptx::tmem_wait_st();
-            // everyone is done reading the stage before it is refilled
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive_local(mdone);
-            if (!wait_bar(c, mdone, ndone & 1u, kErrSoftmax)) return;
-            ++ndone;
           }
-#pragma unroll 1
-          for (int cc = 0; cc < 8; ++cc) {
-            uint32_t o[32];
-            ptx::tmem_ld32(tmem + lane_off + kColO + 32 * cc, o);
-            ptx::tmem_wait_ld();
-            T* dst = orow + 256 * (cc >> 2) + 128 * hf + 32 * (cc & 3);
+          T* dst = orow + d0;
 #pragma unroll
-            for (int g = 0; g < 4; ++g)
-              reinterpret_cast<uint4*>(dst)[g] = make_uint4(
-                  pack2<T>(__uint_as_float(o[8 * g]), __uint_as_float(o[8 * g + 1])),
-                  pack2<T>(__uint_as_float(o[8 * g + 2]), __uint_as_float(o[8 * g + 3])),
-                  pack2<T>(__uint_as_float(o[8 * g + 4]), __uint_as_float(o[8 * g + 5])),
-                  pack2<T>(__uint_as_float(o[8 * g + 6]), __uint_as_float(o[8 * g + 7])));
-          }
-        } else {
-          // rare (a sequence split over three or more pairs): merge from global memory
-#pragma unroll 1
-          for (int cc = 0; cc < 8; ++cc) {
-            const int d0 = 256 * (cc >> 2) + 128 * hf + 32 * (cc & 3);
-            float acc[32];
-#pragma unroll
-            for (int k = 0; k < 32; ++k) acc[k] = 0.f;
-            for (int pp = pf; pp <= pl; ++pp) {
-              const size_t sl = pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp);
-              const float w = exp2f((__ldcg(p.part_lse + sl * kHeads + head) - big) * kLog2e);
-              const float4* src = reinterpret_cast<const float4*>(p.part_o + (sl * kHeads + head) * kDim + d0);
-#pragma unroll
-              for (int g = 0; g < 8; ++g) {
-                const float4 x = __ldcg(src + g);
-                acc[4 * g] = fmaf(w, x.x, acc[4 * g]);
-                acc[4 * g + 1] = fmaf(w, x.y, acc[4 * g + 1]);
-                acc[4 * g + 2] = fmaf(w, x.z, acc[4 * g + 2]);
-                acc[4 * g + 3] = fmaf(w, x.w, acc[4 * g + 3]);
-              }
-            }
-            T* dst = orow + d0;
-#pragma unroll
-            for (int g = 0; g < 4; ++g)
-              reinterpret_cast<uint4*>(dst)[g] =
-                  make_uint4(pack2<T>(acc[8 * g], acc[8 * g + 1]), pack2<T>(acc[8 * g + 2], acc[8 * g + 3]),
-                             pack2<T>(acc[8 * g + 4], acc[8 * g + 5]), pack2<T>(acc[8 * g + 6], acc[8 * g + 7]));
-          }
+          for (int g = 0; g < 4; ++g)
+            reinterpret_cast<uint4*>(dst)[g] =
+                make_uint4(pack2<T>(acc[8 * g], acc[8 * g + 1]), pack2<T>(acc[8 * g + 2], acc[8 * g + 3]),
+                           pack2<T>(acc[8 * g + 4], acc[8 * g + 5]), pack2<T>(acc[8 * g + 6], acc[8 * g + 7]));
         }
-        if (hf == 0 && p.lse_out != nullptr) p.lse_out[(size_t)pc.bb * kHeads + head] = big;
       }
+      if (hf == 0 && p.lse_out != nullptr) p.lse_out[(size_t)pc.bb * kHeads + head] = big;
     }
     ptx::tc_fence_before();
     __syncwarp();
@@ -913,8 +983,10 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
     }
     ptx::mbar_init(ptx::smem_u32(&bars->o_free), 8);
     ptx::mbar_init(ptx::smem_u32(&bars->lx), 4);
-    ptx::mbar_init(ptx::smem_u32(&bars->mg), 4);
-    ptx::mbar_init(ptx::smem_u32(&bars->mg2), 1);
+    ptx::mbar_init(ptx::smem_u32(&bars->stg), 4);
+    ptx::mbar_init(ptx::smem_u32(&bars->stg2), 1);
+    ptx::mbar_init(ptx::smem_u32(&bars->qts), 1);
+    ptx::mbar_init(ptx::smem_u32(&bars->qtr), 4);
     ptx::mbar_init(ptx::smem_u32(&bars->mload), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->mdone), 4);
     ptx::mbar_init(ptx::smem_u32(&bars->drain_qk), 1);
@@ -927,6 +999,8 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
     ptx::prefetch_tensormap(&p.tm_kpe);
     ptx::prefetch_tensormap(&p.tm_q);
     ptx::prefetch_tensormap(&p.tm_qpe);
+    ptx::prefetch_tensormap(&p.tm_out);
+    if (p.part_o != nullptr) ptx::prefetch_tensormap(&p.tm_part);
   }
   if (warp == 1) ptx::tmem_alloc_pair(ptx::smem_u32(tmem_slot), kTmemCols);
   ptx::tc_fence_before();
@@ -1070,13 +1144,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2D row-major [rows, cols] tensor, 64 x 64 boxes, 128-byte swizzle.
-bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, CUtensorMapDataType dt) {
+// 2D row-major [rows, cols] tensor, boxes of 64 rows x 128 bytes, 128-byte swizzle.
+bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, CUtensorMapDataType dt,
+              uint32_t elem_bytes = 2) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {cols * 2};
-  const cuuint32_t box[2] = {64, 64};
+  const cuuint64_t strides[1] = {cols * elem_bytes};
+  const cuuint32_t box[2] = {128 / elem_bytes, 64};
   const cuuint32_t estr[2] = {1, 1};
   return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1184,7 +1259,11 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int) {
   const uint64_t kv_rows = (uint64_t)a.batch * a.seqlen_kv;
   const uint64_t q_rows = (uint64_t)a.batch * kHeads;
   if (!make_map(&p.tm_kv, a.kv, kDim, kv_rows, dt) || !make_map(&p.tm_kpe, a.k_pe, kPeDim, kv_rows, dt) ||
-      !make_map(&p.tm_q, a.q, kDim, q_rows, dt) || !make_map(&p.tm_qpe, a.q_pe, kPeDim, q_rows, dt))
+      !make_map(&p.tm_q, a.q, kDim, q_rows, dt) || !make_map(&p.tm_qpe, a.q_pe, kPeDim, q_rows, dt) ||
+      !make_map(&p.tm_out, a.out, kDim, q_rows, dt))
+    return cudaErrorInvalidValue;
+  if (a.part_o != nullptr &&
+      !make_map(&p.tm_part, a.part_o, kDim, (uint64_t)a.plan.part_rows, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4))
     return cudaErrorInvalidValue;
   p.kv = static_cast<const uint8_t*>(a.kv);
   p.q = static_cast<const uint8_t*>(a.q);

@@ -85,6 +85,36 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst_smem, const void* 
       : "memory");
 }
 
+// 2D tiled load into this CTA's shared memory, completion on this CTA's barrier `bar`.
+__device__ __forceinline__ void tma_load_2d_local(uint32_t dst_smem, const void* desc, uint32_t bar,
+                                                  int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst_smem),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+// 2D tiled store of a shared-memory box to global memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const void* desc, uint32_t src_smem, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(src_smem), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the committed bulk stores have read their shared-memory sources.
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until the committed bulk stores are complete.
+__device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from global memory
 // into this CTA's shared memory, completion counted on the local barrier `bar`.
 __device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes, uint32_t bar) {
