@@ -64,7 +64,7 @@ int resolve(int batch, int heads, int seqlen_kv, const MlaCfg* cfg, Resolved* r)
     set_error("mla: unknown kernel kind %d", kind);
     return MLA_ERR_ARG;
   }
-  const bool tc_ok = sm100_supports(heads, seqlen_kv);
+  const bool tc_ok = sm100_supports(batch, heads, seqlen_kv);
   if (kind == MLA_KERNEL_TC && !tc_ok) {
     set_error("mla: the tensor-core kernel does not cover heads=%d seqlen_kv=%d", heads, seqlen_kv);
     return MLA_ERR_UNSUPPORTED;

@@ -63,10 +63,16 @@ constexpr uint32_t kPBytes = 2 * kChunkBytes;   // one P operand: 64 rows x 128 
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 128;
 constexpr uint32_t kColQT = 384;      // Q dims [0, 256) as bf16/fp16 pairs: 128 columns
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;       // 3 warpgroups
+// Registers per thread after the split: launch budget 384 x 168; producers,
+// issuers and the Q loader need few, the softmax warps many
+// (2 x 128 x kRegsLow + 128 x kRegsSoftmax <= 384 x 168).
+constexpr uint32_t kRegsLow = 88, kRegsSoftmax = 232;
+static_assert(2 * 128 * kRegsLow + 128 * kRegsSoftmax <= 384 * 168, "register split");
 constexpr float kRescaleLog2 = 8.0f;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr int kPrefetchTiles = 2;
+constexpr int kMaxPairs = 256;        // CTA pairs per launch (schedule bound)
 // A merge stages another pair's 64 partial rows (fp32, 2 KB each) in shared memory
 // at this row pitch (16 bytes of padding: threads reading one column of 32 rows
 // hit distinct banks).
@@ -104,6 +110,7 @@ struct Barriers {
   uint64_t xchg[2];
   uint64_t o_done[2], o_free, lx, stg, stg2, mload, mdone;
   uint64_t qts, qtr;     // Q dims [0, 256) staged in shared memory / copied to TMEM
+  uint64_t q_go;         // the first piece's Q loads are issued: K and V loads may start
   uint64_t drain_qk, drain_pv;
 };
 static_assert(sizeof(Barriers) <= 512, "barrier block");
@@ -141,7 +148,7 @@ struct Params {
   float* part_lse;
   uint32_t* status;
   uint32_t* counters;   // [batch][2] pieces finished per (sequence, CTA rank); zero between calls
-  long long total_tiles;
+  uint32_t total_tiles;  // batch x tiles per sequence; total_tiles * (pairs + 1) < 2^32
   int batch, seqlen, nt, pairs, maxp;
   float sl2;            // softmax scale * log2(e)
 };
@@ -158,8 +165,9 @@ __device__ __forceinline__ void raise_abort(const Ctx& c, uint32_t code) {
   if (c.status != nullptr) atomicCAS(c.status, 0u, code);
 }
 
-// Slow path of wait_bar: poll with a time limit.
-__device__ __noinline__ bool wait_bar_slow(const Ctx& c, uint32_t bar, uint32_t parity, uint32_t code) {
+// Slow path of wait_bar: poll with a time limit.  (Inlined: a call out of a
+// setmaxnreg region would have to follow the kernel-wide register budget.)
+__device__ __forceinline__ bool wait_bar_slow(const Ctx& c, uint32_t bar, uint32_t parity, uint32_t code) {
   const uint64_t t0 = ptx::globaltimer();
   for (;;) {
 #pragma unroll 1
@@ -190,19 +198,19 @@ struct Piece {
   bool full;     // the run is the whole sequence
 };
 
-// Iterates the pieces of pair `pair`'s tile range [pair*T/P, (pair+1)*T/P).
+// Iterates the pieces of pair `pair`'s tile range [pair*T/P, (pair+1)*T/P)
+// (32-bit arithmetic: the host keeps T * (P + 1) below 2^32).
 struct PieceIter {
-  long long t, t1;
-  int nt;
-  __device__ PieceIter(const Params& p, int pair) : nt(p.nt) {
-    t = (long long)pair * p.total_tiles / p.pairs;
-    t1 = (long long)(pair + 1) * p.total_tiles / p.pairs;
+  uint32_t t, t1, nt;
+  __device__ PieceIter(const Params& p, int pair) : nt((uint32_t)p.nt) {
+    t = (uint32_t)pair * p.total_tiles / (uint32_t)p.pairs;
+    t1 = (uint32_t)(pair + 1) * p.total_tiles / (uint32_t)p.pairs;
   }
   __device__ bool next(Piece* pc) {
     if (t >= t1) return false;
     pc->bb = (int)(t / nt);
-    const long long bstart = (long long)pc->bb * nt;
-    const long long e = t1 < bstart + nt ? t1 : bstart + nt;
+    const uint32_t bstart = (uint32_t)pc->bb * nt;
+    const uint32_t e = t1 < bstart + nt ? t1 : bstart + nt;
     pc->first = (int)(t - bstart);
     pc->end = (int)(e - bstart);
     pc->full = pc->first == 0 && pc->end == nt;
@@ -226,9 +234,9 @@ struct Ring {
 // Pull this CTA's 64 rows of flattened tile `t` (latent 64 KB, rope 8 KB, both
 // contiguous) into L2, so that the TMA loads of that tile later hit L2: this keeps
 // enough bytes in flight to HBM without spending shared memory on deeper rings.
-__device__ __forceinline__ void prefetch_tile(const Params& p, long long t, uint32_t rank) {
-  const int bb = (int)(t / p.nt);
-  const int jj = (int)(t - (long long)bb * p.nt);
+__device__ __forceinline__ void prefetch_tile(const Params& p, uint32_t t, uint32_t rank) {
+  const int bb = (int)(t / (uint32_t)p.nt);
+  const int jj = (int)(t - (uint32_t)bb * (uint32_t)p.nt);
   const long long row0 = (long long)bb * p.seqlen + (long long)jj * kTile + 64 * (int)rank;
   const long long rows = (long long)bb * p.seqlen + p.seqlen - row0;
   if (rows <= 0) return;
@@ -251,9 +259,12 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
   const uint32_t kempty0 = ptx::smem_u32(&bars->kempty[0]);
   Ring<KS> ring;
   PieceIter it(p, pair);
-  const long long t_end = it.t1;
-  long long t_cur = it.t;
-  for (int d = 0; d < kPrefetchTiles && t_cur + d < t_end; ++d) prefetch_tile(p, t_cur + d, rank);
+  // the first Q rows are requested before any K or V traffic
+  if (!wait_bar(c, ptx::smem_u32(&bars->q_go), 0u, kErrKLoad)) return;
+  const uint32_t t_end = it.t1;
+  uint32_t t_cur = it.t;
+  // (tile 0 is loaded at once; its prefetch would only add requests)
+  for (int d = 1; d < kPrefetchTiles && t_cur + d < t_end; ++d) prefetch_tile(p, t_cur + d, rank);
   Piece pc;
   // K units stream straight across piece boundaries: Q has its own loader thread
   while (it.next(&pc)) {
@@ -304,6 +315,7 @@ __device__ __forceinline__ void q_loader(const Params& p, const Ctx& c, uint32_t
   const uint32_t q_empty = ptx::smem_u32(&bars->q_empty);
   const uint32_t qts = ptx::smem_u32(&bars->qts);
   const uint32_t qtr = ptx::smem_u32(&bars->qtr);
+  const uint32_t q_go = ptx::smem_u32(&bars->q_go);
   PieceIter it(p, pair);
   {
     PieceIter first = it;
@@ -318,17 +330,21 @@ __device__ __forceinline__ void q_loader(const Params& p, const Ctx& c, uint32_t
     if (peek.next(&nxt)) prefetch_q(p, nxt.bb, rank);
     if (piece > 0 && !wait_bar(c, q_empty, (uint32_t)(piece - 1) & 1u, kErrKLoad)) return;
     const int qrow = pc.bb * kHeads + 64 * (int)rank;
+    // the first piece stages dims [0, 256) in the (still unused) P buffers and loads
+    // everything at once; later pieces reuse the Q region once the TMEM copy is made
+    const uint32_t qt_dst = sbase + (piece == 0 ? S::kP : S::kQ);
     ptx::mbar_arrive_expect_tx(qts, 4 * kChunkBytes);
 #pragma unroll 1
     for (int ch = 0; ch < 4; ++ch)
-      ptx::tma_load_2d_local(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, qts, 64 * ch, qrow);
-    if (!wait_bar(c, qtr, (uint32_t)piece & 1u, kErrKLoad)) return;
+      ptx::tma_load_2d_local(qt_dst + ch * kChunkBytes, &p.tm_q, qts, 64 * ch, qrow);
+    if (piece > 0 && !wait_bar(c, qtr, (uint32_t)piece & 1u, kErrKLoad)) return;
     if (leader) ptx::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
 #pragma unroll 1
     for (int ch = 0; ch < 4; ++ch)
       ptx::tma_load_2d_pair(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, q_full_leader, kQTDims + 64 * ch,
                             qrow);
     ptx::tma_load_2d_pair(sbase + S::kQ + 4 * kChunkBytes, &p.tm_qpe, q_full_leader, 0, qrow);
+    if (piece == 0) ptx::mbar_arrive_local(q_go);
     ++piece;
   }
 }
@@ -348,6 +364,7 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
   const uint32_t vempty0 = ptx::smem_u32(&bars->vempty[0]);
   Ring<VS> ring;
   PieceIter it(p, pair);
+  if (!wait_bar(c, ptx::smem_u32(&bars->q_go), 0u, kErrVLoad)) return;
   Piece pc;
   while (it.next(&pc)) {
 #pragma unroll 1
@@ -505,29 +522,27 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 // Workspace slot of sequence bb's piece inside pair pp's range.
-__device__ __forceinline__ size_t pair_slot(int pp, int bb, long long total_tiles, int pairs, int nt,
+__device__ __forceinline__ size_t pair_slot(int pp, int bb, uint32_t total_tiles, int pairs, int nt,
                                             int maxp) {
-  return (size_t)pp * maxp + (bb - (int)((long long)pp * total_tiles / pairs / nt));
+  return (size_t)pp * maxp + (bb - (int)((uint32_t)pp * total_tiles / (uint32_t)pairs / (uint32_t)nt));
 }
 
 // First and last pair whose tile range [p*T/P, (p+1)*T/P) meets sequence bb.
-__device__ __forceinline__ void pairs_of_sequence(long long total_tiles, int pairs, int nt, int bb,
+__device__ __forceinline__ void pairs_of_sequence(uint32_t total_tiles, int pairs, int nt, int bb,
                                                   int* pf, int* pl) {
-  const long long x0 = (long long)bb * nt;
-  *pf = (int)(((x0 + 1) * pairs + total_tiles - 1) / total_tiles) - 1;
-  *pl = (int)(((x0 + nt) * pairs + total_tiles - 1) / total_tiles) - 1;
+  const uint32_t x0 = (uint32_t)bb * (uint32_t)nt;
+  *pf = (int)(((x0 + 1) * (uint32_t)pairs + total_tiles - 1) / total_tiles) - 1;
+  *pl = (int)(((x0 + (uint32_t)nt) * (uint32_t)pairs + total_tiles - 1) / total_tiles) - 1;
 }
 
-// Copy this CTA's staged Q rows, latent dims [0, 256) (four SW128 boxes at the
-// start of the Q region), into TMEM as the A operand of the first 16 QK^T
+// Copy this CTA's staged Q rows, latent dims [0, 256) (four SW128 boxes at
+// `src`: the P buffers for the first piece, else the start of the Q region), into TMEM as the A operand of the first 16 QK^T
 // k-steps: lane L <- row L % 64, so both lane halves hold the rows (the
 // duplicated layout of a pair MMA's A operand in TMEM).
-template <typename T>
-__device__ __forceinline__ void copy_qt(const uint8_t* smem, int m, uint32_t tmem, uint32_t lane_off) {
-  using S = Smem<T>;
+__device__ __forceinline__ void copy_qt(const uint8_t* src, int m, uint32_t tmem, uint32_t lane_off) {
 #pragma unroll
   for (int ch = 0; ch < 4; ++ch) {
-    const uint8_t* row = smem + S::kQ + ch * kChunkBytes + m * 128;
+    const uint8_t* row = src + ch * kChunkBytes + m * 128;
     uint32_t w[32];
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
@@ -604,7 +619,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
   // Q dims [0, 256) of piece `k`, staged by the Q loader, into TMEM
   auto take_qt = [&](int k) -> bool {
     if (!wait_bar(c, qts, (uint32_t)k & 1u, kErrSoftmax)) return false;
-    copy_qt<T>(smem, m, tmem, lane_off);
+    copy_qt(smem + (k == 0 ? S::kP : S::kQ), m, tmem, lane_off);
     ptx::tc_fence_before();
     __syncwarp();
     if (lane == 0) {
@@ -945,7 +960,8 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
 
 // ---------------------------------------------------------------------------
 // the kernel: warp 0 K producer, warp 1 TMEM owner + QK^T issuer, warp 2 V
-// producer, warp 3 P.V issuer, warps 4..7 softmax/epilogue
+// producer, warp 3 P.V issuer, warps 4..7 softmax/epilogue, warp 8 Q loader
+// (warps 9..11 complete the third warpgroup)
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -987,6 +1003,7 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
     ptx::mbar_init(ptx::smem_u32(&bars->stg2), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->qts), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->qtr), 4);
+    ptx::mbar_init(ptx::smem_u32(&bars->q_go), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->mload), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->mdone), 4);
     ptx::mbar_init(ptx::smem_u32(&bars->drain_qk), 1);
@@ -1013,9 +1030,18 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
   c.abort_peer = ptx::mapa(ptx::smem_u32(abort_flag), rank ^ 1u);
   c.status = p.status;
 
+  // One role per warp: a lane blocked in mbarrier.try_wait holds back every
+  // other lane of its warp.  Warpgroup 1 (warps 4..7) runs the softmax.
+  if ((warp >> 2) == 1) {
+    ptx::setmaxnreg_inc<kRegsSoftmax>();
+    softmax_epilogue<T>(p, c, rank, pair, smem, tmem, bars, warp & 3, lane);
+    ptx::setmaxnreg_dec<kRegsLow>();   // same budget as the other warps from here on
+  } else {
+    ptx::setmaxnreg_dec<kRegsLow>();
   if (warp == 0) {
     if (lane == 0) k_producer<T>(p, c, rank, pair, sbase, bars);
-    else if (lane == 16) q_loader<T>(p, c, rank, pair, sbase, bars);
+  } else if (warp == 8) {
+    if (lane == 0) q_loader<T>(p, c, rank, pair, sbase, bars);
   } else if (warp == 1) {
     if (rank == 0 && lane == 0) {
       qk_issuer<T>(p, c, pair, sbase, tmem, bars);
@@ -1031,8 +1057,7 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
       ptx::mma_commit_pair_mc(ptx::smem_u32(&bars->drain_pv), 0x1);
       wait_bar(c, ptx::smem_u32(&bars->drain_pv), 0u, kErrDrain);
     }
-  } else {
-    softmax_epilogue<T>(p, c, rank, pair, smem, tmem, bars, warp & 3, lane);
+  }
   }
   __syncwarp();
   if (aborted(c)) {
@@ -1048,83 +1073,6 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
     ptx::tmem_dealloc_pair(tmem, kTmemCols);
     ptx::tmem_relinquish_pair();
   }
-}
-
-// ---------------------------------------------------------------------------
-// combine for the pair schedule: one 128-thread CTA per (head, sequence);
-// sequences that one pair covered whole were written directly and are skipped.
-// Same LSE algebra as mla_combine.cu (mla_decode.py:212-246).
-// ---------------------------------------------------------------------------
-constexpr int kMaxPairs = 256;   // pairs per launch (schedule bound)
-
-template <typename T>
-__global__ void __launch_bounds__(128)
-mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__ part_o,
-                        T* __restrict__ out, float* __restrict__ lse_out, long long total_tiles,
-                        int nt, int pairs, int maxp) {
-  const int head = blockIdx.x, bb = blockIdx.y, tid = threadIdx.x;
-  const long long x0 = (long long)bb * nt;
-  (void)x0;
-  int pf, pl;
-  pairs_of_sequence(total_tiles, pairs, nt, bb, &pf, &pl);
-  if (pf == pl) return;   // one pair covered the whole sequence and wrote `out` itself
-  const int n = pl - pf + 1;
-  // Every thread loads the (few) split LSEs itself -- broadcast loads, issued together --
-  // and its 4 columns of every partial row, then merges; no serial thread-0 phase.
-  constexpr int kFast = 8;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float lse;
-  if (n <= kFast) {
-    float lk[kFast];
-    float4 vk[kFast];
-#pragma unroll
-    for (int k = 0; k < kFast; ++k) {
-      if (k < n) {
-        const size_t sl = pair_slot(pf + k, bb, total_tiles, pairs, nt, maxp);
-        lk[k] = __ldg(part_lse + sl * kHeads + head);
-        vk[k] = __ldg(reinterpret_cast<const float4*>(part_o + (sl * kHeads + head) * kDim) + tid);
-      } else {
-        lk[k] = -INFINITY;
-        vk[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
-    float mx = lk[0];
-#pragma unroll
-    for (int k = 1; k < kFast; ++k) mx = fmaxf(mx, lk[k]);
-    float sum = 0.f;
-#pragma unroll
-    for (int k = 0; k < kFast; ++k) sum += exp2f((lk[k] - mx) * kLog2e);
-    lse = mx + logf(sum);
-#pragma unroll
-    for (int k = 0; k < kFast; ++k) {
-      const float w = exp2f((lk[k] - lse) * kLog2e);
-      acc.x = fmaf(w, vk[k].x, acc.x);
-      acc.y = fmaf(w, vk[k].y, acc.y);
-      acc.z = fmaf(w, vk[k].z, acc.z);
-      acc.w = fmaf(w, vk[k].w, acc.w);
-    }
-  } else {
-    float mx = -INFINITY;
-    for (int k = 0; k < n; ++k) mx = fmaxf(mx, __ldg(part_lse + pair_slot(pf + k, bb, total_tiles, pairs, nt, maxp) * kHeads + head));
-    float sum = 0.f;
-    for (int k = 0; k < n; ++k)
-      sum += exp2f((__ldg(part_lse + pair_slot(pf + k, bb, total_tiles, pairs, nt, maxp) * kHeads + head) - mx) * kLog2e);
-    lse = mx + logf(sum);
-    for (int k = 0; k < n; ++k) {
-      const size_t sl = pair_slot(pf + k, bb, total_tiles, pairs, nt, maxp);
-      const float w = exp2f((__ldg(part_lse + sl * kHeads + head) - lse) * kLog2e);
-      const float4 v = __ldg(reinterpret_cast<const float4*>(part_o + (sl * kHeads + head) * kDim) + tid);
-      acc.x = fmaf(w, v.x, acc.x);
-      acc.y = fmaf(w, v.y, acc.y);
-      acc.z = fmaf(w, v.z, acc.z);
-      acc.w = fmaf(w, v.w, acc.w);
-    }
-  }
-  uint2 o;
-  o.x = pack2<T>(acc.x, acc.y);
-  o.y = pack2<T>(acc.z, acc.w);
-  reinterpret_cast<uint2*>(out + ((size_t)bb * kHeads + head) * kDim)[tid] = o;
-  if (lse_out != nullptr && tid == 0) lse_out[(size_t)bb * kHeads + head] = lse;
 }
 
 // ---------------------------------------------------------------------------
@@ -1214,7 +1162,13 @@ int current_max_pairs() {
 
 }  // namespace sm100
 
-bool sm100_supports(int heads, int seqlen_kv) { return heads == sm100::kHeads && seqlen_kv >= 1; }
+bool sm100_supports(int batch, int heads, int seqlen_kv) {
+  // 32-bit tile arithmetic in the kernel and int32 TMA row coordinates
+  const long long nt = (seqlen_kv + sm100::kTile - 1) / sm100::kTile;
+  return heads == sm100::kHeads && seqlen_kv >= 1 && batch >= 1 &&
+         (long long)batch * nt * (sm100::kMaxPairs + 1) < (1ll << 32) &&
+         (long long)batch * seqlen_kv < (1ll << 31) - sm100::kTile;
+}
 
 SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int* variant) {
   (void)heads;
@@ -1278,7 +1232,7 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int) {
   p.batch = a.batch;
   p.seqlen = a.seqlen_kv;
   p.nt = (a.seqlen_kv + kTile - 1) / kTile;
-  p.total_tiles = (long long)a.batch * p.nt;
+  p.total_tiles = (uint32_t)a.batch * (uint32_t)p.nt;
   p.pairs = pairs;
   p.maxp = a.plan.extra;
   p.sl2 = a.softmax_scale * kLog2e;
@@ -1287,21 +1241,6 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int) {
         <<<2 * pairs, kThreads, Smem<__nv_bfloat16>::kBytes, a.stream>>>(p);
   else
     mla_sm100_decode_kernel<__half><<<2 * pairs, kThreads, Smem<__half>::kBytes, a.stream>>>(p);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_sm100_combine(const DecodeArgs& a) {
-  using namespace sm100;
-  const int nt = (a.seqlen_kv + kTile - 1) / kTile;
-  const long long total = (long long)a.batch * nt;
-  const dim3 grid(kHeads, a.batch);
-  if (a.dtype == MLA_DTYPE_BF16)
-    mla_pair_combine_kernel<__nv_bfloat16><<<grid, 128, 0, a.stream>>>(
-        a.part_lse, a.part_o, static_cast<__nv_bfloat16*>(a.out), a.lse, total, nt, a.plan.bpc,
-        a.plan.extra);
-  else
-    mla_pair_combine_kernel<__half><<<grid, 128, 0, a.stream>>>(
-        a.part_lse, a.part_o, static_cast<__half*>(a.out), a.lse, total, nt, a.plan.bpc, a.plan.extra);
   return cudaGetLastError();
 }
 

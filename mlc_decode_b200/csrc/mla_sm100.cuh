@@ -6,15 +6,12 @@
 namespace mla {
 
 // True when the tensor-core kernel covers this shape.
-bool sm100_supports(int heads, int seqlen_kv);
+bool sm100_supports(int batch, int heads, int seqlen_kv);
 
 // Split plan (and kernel variant) the tensor-core kernel uses for this shape.
 SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int* variant);
 
 // Enqueue the tensor-core split-KV kernel; partials go to a.part_o/a.part_lse.
 cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant);
-
-// Enqueue the combine of the tensor-core kernel's pair-schedule partials.
-cudaError_t launch_sm100_combine(const DecodeArgs& a);
 
 }  // namespace mla

@@ -85,6 +85,16 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst_smem, const void* 
       : "memory");
 }
 
+// Per-warpgroup register budget (every warp of the warpgroup executes it).
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 // 2D tiled load into this CTA's shared memory, completion on this CTA's barrier `bar`.
 __device__ __forceinline__ void tma_load_2d_local(uint32_t dst_smem, const void* desc, uint32_t bar,
                                                   int32_t x, int32_t y) {
