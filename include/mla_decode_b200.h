@@ -29,7 +29,11 @@ extern "C" {
 
 #define MLA_ABI_VERSION 1
 
-enum MlaDtype { MLA_DTYPE_F16 = 0, MLA_DTYPE_BF16 = 1 };
+enum MlaDtype {
+  MLA_DTYPE_F16 = 0,
+  MLA_DTYPE_BF16 = 1,
+  MLA_DTYPE_F32 = 2   /* output only: mla_combine's `out`, mla_decode_partial's `o` */
+};
 
 enum MlaStatus {
   MLA_OK = 0,
@@ -95,7 +99,9 @@ size_t mla_workspace_bytes(int32_t batch, int32_t heads, int32_t seqlen_kv,
  * Facts about the plan mla_decode_fwd would use for this shape and config:
  *   out4[0] kernel (enum MlaKernelKind, never AUTO)
  *   out4[1] KV splits per sequence (CUDA-core kernel) or CTA pairs (tensor-core kernel)
- *   out4[2] kernel launches per call (1 or 2)
+ *   out4[2] kernel launches per call (1 or 2; the tensor-core kernel merges a
+ *           sequence split between a few CTA pairs itself, and leaves sequences
+ *           split between many pairs to a combine launch)
  *   out4[3] bytes at the start of the workspace that must be zero before the
  *           first call with it (the tensor-core kernel's status word and piece
  *           counters; every call leaves them zero again)
@@ -144,12 +150,31 @@ int32_t mla_decode_combine_ws(void* out, float* lse, const void* workspace,
  *   part_lse [num_split, batch, heads]       float32 (-inf = empty split)
  *   part_o   [num_split, batch, heads, 512]  float32
  * out[b,h,:] = sum_k exp(lse_k - LSE) * o_k with LSE = logsumexp_k(lse_k);
- * lse (optional) receives LSE.  Also merges per-GPU results of a
- * sequence-split decode after they are gathered into one buffer.
+ * lse (optional) receives LSE.  dtype is the type of `out`: F16, BF16, or F32
+ * (a float32 result that can itself be combined again).  Also merges per-GPU
+ * results of a sequence-split decode (mla_decode_partial on each GPU's part
+ * of the KV sequence) after they are gathered into one buffer.
  */
 int32_t mla_combine(const float* part_lse, const float* part_o,
                     int32_t num_split, int32_t batch, int32_t heads,
                     void* out, float* lse, int32_t dtype, void* stream);
+
+/*
+ * mla_decode_fwd for one contiguous part of every sequence's KV cache, with a
+ * float32 result: o[b,h,:] (float32 [batch, heads, 512], normalised) and
+ * lse[b,h] (float32 [batch, heads], natural log, required) are the decode of
+ * q against rows [0, seqlen_kv) of kv/k_pe.  Results of several parts of the
+ * same sequences, stacked as [parts, batch, heads, ...], combine into the
+ * decode over the whole sequence with mla_combine (the sequence split across
+ * GPUs).  Same inputs, workspace and checks as mla_decode_fwd.  No
+ * counterpart in the reference, which splits a sequence only inside one
+ * launch (the num_split partials of mla_decode.py:73-76).
+ */
+int32_t mla_decode_partial(const void* q, const void* q_pe, const void* kv,
+                           const void* k_pe, float* o, float* lse,
+                           void* workspace, size_t workspace_bytes,
+                           int32_t batch, int32_t heads, int32_t seqlen_kv,
+                           int32_t dtype, const MlaCfg* cfg, void* stream);
 
 /*
  * mla_decode_fwd without a workspace argument, for callers that cannot

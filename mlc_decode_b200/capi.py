@@ -13,6 +13,7 @@ from . import build as _build
 
 MLA_DTYPE_F16 = 0
 MLA_DTYPE_BF16 = 1
+MLA_DTYPE_F32 = 2      # output only (mla_combine, mla_decode_partial)
 
 MLA_KERNEL_AUTO = 0
 MLA_KERNEL_SIMT = 1
@@ -24,7 +25,7 @@ STATUS_NAMES = {0: "MLA_OK", 1: "MLA_ERR_ARG", 2: "MLA_ERR_WORKSPACE", 3: "MLA_E
 EXPORTED_SYMBOLS = ("mla_abi_version", "mla_last_error", "mla_split_plan",
                     "mla_workspace_bytes", "mla_decode_fwd", "mla_decode_splitkv",
                     "mla_decode_combine_ws", "mla_combine", "mla_decode_fwd_noalloc",
-                    "mla_describe_plan")
+                    "mla_describe_plan", "mla_decode_partial")
 
 
 class MlaCfg(ctypes.Structure):
@@ -82,6 +83,8 @@ def load(build_if_missing: bool = True):
         lib.mla_decode_fwd.restype = i32
         lib.mla_decode_splitkv.argtypes = lib.mla_decode_fwd.argtypes
         lib.mla_decode_splitkv.restype = i32
+        lib.mla_decode_partial.argtypes = lib.mla_decode_fwd.argtypes
+        lib.mla_decode_partial.restype = i32
         lib.mla_decode_combine_ws.argtypes = [vp, vp, vp, sz, i32, i32, i32, i32,
                                               ctypes.POINTER(MlaCfg), vp]
         lib.mla_decode_combine_ws.restype = i32
@@ -162,6 +165,13 @@ def decode_fwd_noalloc(q, q_pe, kv, k_pe, out, lse, batch, heads, seqlen_kv, dty
     """mla_decode_fwd_noalloc: scratch from the library's static device array (no allocation)."""
     check(load().mla_decode_fwd_noalloc(q, q_pe, kv, k_pe, out, lse, int(batch), int(heads),
                                         int(seqlen_kv), int(dtype), ctypes.byref(cfg), stream))
+
+
+def decode_partial(q, q_pe, kv, k_pe, o, lse, ws, ws_bytes, batch, heads, seqlen_kv, dtype,
+                   cfg: MlaCfg, stream) -> None:
+    """mla_decode_partial: float32 normalised O and natural-log LSE of this KV part."""
+    check(load().mla_decode_partial(q, q_pe, kv, k_pe, o, lse, ws, ws_bytes, int(batch), int(heads),
+                                    int(seqlen_kv), int(dtype), ctypes.byref(cfg), stream))
 
 
 def decode_splitkv(q, q_pe, kv, k_pe, out, lse, ws, ws_bytes, batch, heads, seqlen_kv, dtype,

@@ -162,7 +162,7 @@ int32_t mla_describe_plan(int32_t batch, int32_t heads, int32_t seqlen_kv, int32
   const bool tc = r.kernel == MLA_KERNEL_TC;
   out4[0] = r.kernel;
   out4[1] = tc ? r.plan.bpc : r.plan.ns;
-  out4[2] = (!tc && r.plan.needs_combine) ? 2 : 1;
+  out4[2] = (r.plan.needs_combine && (!tc || r.tc_variant == 1)) ? 2 : 1;
   out4[3] = tc ? (int64_t)(kStatusBytes + counter_bytes(batch)) : 0;
   return MLA_OK;
 }
@@ -213,6 +213,7 @@ int prepare(const char* fn, const void* q, const void* q_pe, const void* kv, con
   a->kv = kv;
   a->k_pe = k_pe;
   a->out = out;
+  a->out_dtype = dtype;
   a->lse = lse;
   a->batch = batch;
   a->heads = heads;
@@ -253,11 +254,14 @@ int run_splitkv(const char* fn, const DecodeArgs& a, const Resolved& r) {
 }
 
 int run_combine_ws(const char* fn, const DecodeArgs& a, const Resolved& r) {
-  // the decode kernel wrote out/lse itself: single-split plans, and the tensor-core
-  // kernel, whose epilogue merges split sequences
-  if (!r.plan.needs_combine || r.kernel == MLA_KERNEL_TC) return MLA_OK;
-  const cudaError_t err = launch_combine(a.part_lse, a.part_o, r.plan.ns, a.batch, a.heads, a.out,
-                                         a.lse, a.dtype, a.stream);
+  // the decode kernel wrote out/lse itself: single-split plans, and tensor-core
+  // plans whose sequences are split between a few CTA pairs (merged in-kernel)
+  if (!r.plan.needs_combine || (r.kernel == MLA_KERNEL_TC && r.tc_variant == 0)) return MLA_OK;
+  const cudaError_t err =
+      r.kernel == MLA_KERNEL_TC
+          ? launch_sm100_combine(a)
+          : launch_combine(a.part_lse, a.part_o, r.plan.ns, a.batch, a.heads, a.out, a.lse,
+                           a.out_dtype, a.stream);
   if (err != cudaSuccess) {
     set_error("%s: combine launch failed: %s", fn, cudaGetErrorString(err));
     return MLA_ERR_CUDA;
@@ -283,6 +287,26 @@ int32_t mla_decode_fwd(const void* q, const void* q_pe, const void* kv, const vo
   rc = run_splitkv("mla_decode_fwd", a, r);
   if (rc != MLA_OK) return rc;
   return run_combine_ws("mla_decode_fwd", a, r);
+}
+
+int32_t mla_decode_partial(const void* q, const void* q_pe, const void* kv, const void* k_pe,
+                           float* o, float* lse, void* workspace, size_t workspace_bytes,
+                           int32_t batch, int32_t heads, int32_t seqlen_kv, int32_t dtype,
+                           const MlaCfg* cfg, void* stream) {
+  if (lse == nullptr) {
+    set_error("mla_decode_partial: lse is required");
+    return MLA_ERR_ARG;
+  }
+  DecodeArgs a;
+  Resolved r;
+  size_t need = 0;
+  int rc = prepare("mla_decode_partial", q, q_pe, kv, k_pe, o, lse, workspace, workspace_bytes, batch,
+                   heads, seqlen_kv, dtype, cfg, stream, true, &a, &r, &need);
+  if (rc != MLA_OK) return rc;
+  a.out_dtype = MLA_DTYPE_F32;
+  rc = run_splitkv("mla_decode_partial", a, r);
+  if (rc != MLA_OK) return rc;
+  return run_combine_ws("mla_decode_partial", a, r);
 }
 
 int32_t mla_decode_splitkv(const void* q, const void* q_pe, const void* kv, const void* k_pe,
@@ -322,8 +346,8 @@ int32_t mla_combine(const float* part_lse, const float* part_o, int32_t num_spli
     set_error("mla_combine: bad num_split/batch/heads (%d, %d, %d)", num_split, batch, heads);
     return MLA_ERR_ARG;
   }
-  if (dtype != MLA_DTYPE_F16 && dtype != MLA_DTYPE_BF16) {
-    set_error("mla_combine: dtype must be 0 or 1");
+  if (dtype != MLA_DTYPE_F16 && dtype != MLA_DTYPE_BF16 && dtype != MLA_DTYPE_F32) {
+    set_error("mla_combine: dtype must be 0, 1 or 2");
     return MLA_ERR_ARG;
   }
   if (!aligned16(part_o) || !aligned16(out)) {

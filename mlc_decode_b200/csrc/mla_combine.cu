@@ -46,6 +46,11 @@ __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* dst, float4
   *reinterpret_cast<uint2*>(dst) = w;
 }
 
+template <>
+__device__ __forceinline__ void store4<float>(float* dst, float4 v) {
+  *reinterpret_cast<float4*>(dst) = v;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
 mla_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__ part_o,
@@ -129,6 +134,9 @@ cudaError_t launch_combine(const float* part_lse, const float* part_o, int ns, i
   if (dtype == MLA_DTYPE_F16) {
     mla_combine_kernel<__half><<<rows, kThreads, smem, stream>>>(
         part_lse, part_o, ns, rows, static_cast<__half*>(out), lse);
+  } else if (dtype == MLA_DTYPE_F32) {
+    mla_combine_kernel<float><<<rows, kThreads, smem, stream>>>(
+        part_lse, part_o, ns, rows, static_cast<float*>(out), lse);
   } else {
     mla_combine_kernel<__nv_bfloat16><<<rows, kThreads, smem, stream>>>(
         part_lse, part_o, ns, rows, static_cast<__nv_bfloat16*>(out), lse);

@@ -110,6 +110,7 @@ struct DecodeArgs {
   const void* kv;
   const void* k_pe;
   void* out;          // final output (used when ns == 1)
+  int out_dtype;      // MlaDtype of `out`: dtype, or MLA_DTYPE_F32 (mla_decode_partial)
   float* lse;         // optional final lse (natural log)
   float* part_o;      // [ns, batch, heads, 512]
   float* part_lse;    // [ns, batch, heads]

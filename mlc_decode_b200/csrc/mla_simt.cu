@@ -34,10 +34,10 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
 mla_simt_splitkv_kernel(const T* __restrict__ q, const T* __restrict__ q_pe,
                         const T* __restrict__ kv, const T* __restrict__ k_pe,
-                        T* __restrict__ out, float* __restrict__ lse_out,
+                        void* __restrict__ out, float* __restrict__ lse_out,
                         float* __restrict__ part_o, float* __restrict__ part_lse,
                         int batch, int heads, int seqlen_kv, int ns, int bpc, int extra,
-                        int block_n, float scale_log2) {
+                        int block_n, float scale_log2, bool out_f32) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* sQ = reinterpret_cast<float*>(smem_raw);
   uint16_t* sK = reinterpret_cast<uint16_t*>(sQ + kHeadsPerCta * kQStride);
@@ -144,10 +144,16 @@ mla_simt_splitkv_kernel(const T* __restrict__ q, const T* __restrict__ q_pe,
   const float inv = empty ? 0.f : 1.f / l;
   const float lse_nat = empty ? -INFINITY : (m * scale_log2 + log2f(l)) * kLn2;
   if (ns == 1) {
-    uint32_t* orow = reinterpret_cast<uint32_t*>(out + row * kDim);
+    if (out_f32) {
+      float2* orow = reinterpret_cast<float2*>(static_cast<float*>(out) + row * kDim);
 #pragma unroll
-    for (int k = 0; k < 16; ++k)
-      orow[l16 + 16 * k] = Elt<T>::pack2(o[2 * k] * inv, o[2 * k + 1] * inv);
+      for (int k = 0; k < 16; ++k) orow[l16 + 16 * k] = make_float2(o[2 * k] * inv, o[2 * k + 1] * inv);
+    } else {
+      uint32_t* orow = reinterpret_cast<uint32_t*>(static_cast<T*>(out) + row * kDim);
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        orow[l16 + 16 * k] = Elt<T>::pack2(o[2 * k] * inv, o[2 * k + 1] * inv);
+    }
     if (lse_out != nullptr && l16 == 0) lse_out[row] = lse_nat;
   } else {
     const size_t prow = (size_t)z * batch * heads + row;
@@ -174,9 +180,9 @@ cudaError_t launch_typed(const DecodeArgs& a) {
   const float scale_log2 = a.softmax_scale * kLog2e;
   mla_simt_splitkv_kernel<T><<<grid, kThreads, kSmemBytes, a.stream>>>(
       static_cast<const T*>(a.q), static_cast<const T*>(a.q_pe), static_cast<const T*>(a.kv),
-      static_cast<const T*>(a.k_pe), static_cast<T*>(a.out), a.lse, a.part_o, a.part_lse,
+      static_cast<const T*>(a.k_pe), a.out, a.lse, a.part_o, a.part_lse,
       a.batch, a.heads, a.seqlen_kv, a.plan.ns, a.plan.bpc, a.plan.extra, a.plan.block_n,
-      scale_log2);
+      scale_log2, a.out_dtype == MLA_DTYPE_F32);
   return cudaGetLastError();
 }
 

@@ -73,6 +73,7 @@ constexpr float kRescaleLog2 = 8.0f;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr int kPrefetchTiles = 2;
 constexpr int kMaxPairs = 256;        // CTA pairs per launch (schedule bound)
+constexpr int kFuseMaxPieces = 3;     // most pieces of one sequence merged in-kernel
 // A merge stages another pair's 64 partial rows (fp32, 2 KB each) in shared memory
 // at this row pitch (16 bytes of padding: threads reading one column of 32 rows
 // hit distinct banks).
@@ -150,6 +151,8 @@ struct Params {
   uint32_t* counters;   // [batch][2] pieces finished per (sequence, CTA rank); zero between calls
   uint32_t total_tiles;  // batch x tiles per sequence; total_tiles * (pairs + 1) < 2^32
   int batch, seqlen, nt, pairs, maxp;
+  int out_f32;          // `out` is float32 (tm_out then has 32 x 64 float boxes)
+  int fuse_merge;       // merge split sequences here (last arriver); else a combine launch does
   float sl2;            // softmax scale * log2(e)
 };
 
@@ -234,14 +237,15 @@ struct Ring {
 // Pull this CTA's 64 rows of flattened tile `t` (latent 64 KB, rope 8 KB, both
 // contiguous) into L2, so that the TMA loads of that tile later hit L2: this keeps
 // enough bytes in flight to HBM without spending shared memory on deeper rings.
-__device__ __forceinline__ void prefetch_tile(const Params& p, uint32_t t, uint32_t rank) {
+__device__ __forceinline__ void prefetch_tile(const Params& p, uint32_t t, uint32_t rank,
+                                              uint64_t keep) {
   const int bb = (int)(t / (uint32_t)p.nt);
   const int jj = (int)(t - (uint32_t)bb * (uint32_t)p.nt);
   const long long row0 = (long long)bb * p.seqlen + (long long)jj * kTile + 64 * (int)rank;
   const long long rows = (long long)bb * p.seqlen + p.seqlen - row0;
   if (rows <= 0) return;
   const uint32_t n = rows < 64 ? (uint32_t)rows : 64u;
-  ptx::prefetch_l2(p.kv + row0 * (kDim * 2), n * (kDim * 2));
+  ptx::prefetch_l2_hint(p.kv + row0 * (kDim * 2), n * (kDim * 2), keep);   // read by K and V
   ptx::prefetch_l2(p.kpe + row0 * (kPeDim * 2), n * (kPeDim * 2));
 }
 
@@ -264,13 +268,17 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
   const uint32_t t_end = it.t1;
   uint32_t t_cur = it.t;
   // (tile 0 is loaded at once; its prefetch would only add requests)
-  for (int d = 1; d < kPrefetchTiles && t_cur + d < t_end; ++d) prefetch_tile(p, t_cur + d, rank);
+  // latent rows are read twice (K now, V one tile later): keep them in L2;
+  // rope rows are read once
+  const uint64_t keep = ptx::l2_policy_evict_last();
+  const uint64_t once = ptx::l2_policy_evict_first();
+  for (int d = 1; d < kPrefetchTiles && t_cur + d < t_end; ++d) prefetch_tile(p, t_cur + d, rank, keep);
   Piece pc;
   // K units stream straight across piece boundaries: Q has its own loader thread
   while (it.next(&pc)) {
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j, ++t_cur) {
-      if (t_cur + kPrefetchTiles < t_end) prefetch_tile(p, t_cur + kPrefetchTiles, rank);
+      if (t_cur + kPrefetchTiles < t_end) prefetch_tile(p, t_cur + kPrefetchTiles, rank, keep);
       const int y = pc.bb * p.seqlen + j * kTile + 64 * (int)rank;
 #pragma unroll 1
       for (int u = 0; u < 5; ++u) {
@@ -280,10 +288,10 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
         const uint32_t dst = sbase + S::kKRing + ring.stage * kStageBytes;
         const uint32_t bar = kfull0_leader + 8 * ring.stage;
         if (u < 4) {
-          ptx::tma_load_2d_pair(dst, &p.tm_kv, bar, 128 * u, y);
-          ptx::tma_load_2d_pair(dst + kChunkBytes, &p.tm_kv, bar, 128 * u + 64, y);
+          ptx::tma_load_2d_pair_hint(dst, &p.tm_kv, bar, 128 * u, y, keep);
+          ptx::tma_load_2d_pair_hint(dst + kChunkBytes, &p.tm_kv, bar, 128 * u + 64, y, keep);
         } else {
-          ptx::tma_load_2d_pair(dst, &p.tm_kpe, bar, 0, y);
+          ptx::tma_load_2d_pair_hint(dst, &p.tm_kpe, bar, 0, y, once);
         }
         ring.advance();
       }
@@ -359,6 +367,7 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
   using S = Smem<T>;
   constexpr int VS = Cfg<T>::kVStages;
   const bool leader = rank == 0;
+  const uint64_t once = ptx::l2_policy_evict_first();
   const uint32_t vfull0 = ptx::smem_u32(&bars->vfull[0]);
   const uint32_t vfull0_leader = ptx::mapa(vfull0, 0);
   const uint32_t vempty0 = ptx::smem_u32(&bars->vempty[0]);
@@ -378,8 +387,9 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
         const uint32_t dst = sbase + S::kVRing + ring.stage * kStageBytes;
         const uint32_t bar = vfull0_leader + 8 * ring.stage;
         const int x = 256 * nh + 128 * (int)rank;
-        ptx::tma_load_2d_pair(dst, &p.tm_kv, bar, x, y0 + 64 * th);
-        ptx::tma_load_2d_pair(dst + kChunkBytes, &p.tm_kv, bar, x + 64, y0 + 64 * th);
+        // the latent rows' last read
+        ptx::tma_load_2d_pair_hint(dst, &p.tm_kv, bar, x, y0 + 64 * th, once);
+        ptx::tma_load_2d_pair_hint(dst + kChunkBytes, &p.tm_kv, bar, x + 64, y0 + 64 * th, once);
         ring.advance();
       }
     }
@@ -630,7 +640,39 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
   };
   // stage O (TMEM) x scale as the output rows of this CTA's heads and store them
   // with TMA; output chunk co = (nh, bx) of a thread is dims 256 nh + 128 hf + 64 bx
+  // stage O (TMEM) x scale as float32 rows and store them with TMA to rows
+  // [y, y + 64) of `map`; fp32 chunk ci = (nh, k) of a thread is dims
+  // 256 nh + 128 hf + 32 k
+  auto store_rows_f32 = [&](const CUtensorMap* map, int y, float scale) -> bool {
+#pragma unroll 1
+    for (int r = 0; r < 8 / kHB; ++r) {
+#pragma unroll 1
+      for (int i = 0; i < kHB; ++i) {
+        const int ci = r * kHB + i;
+        uint32_t o[32];
+        ptx::tmem_ld32(tmem + lane_off + kColO + 32 * ci, o);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * scale);
+        st_box_row(stage + (hf * kHB + i) * kChunkBytes, m, o);
+      }
+      ptx::fence_proxy_async_smem();
+      if (!sync4(stg, n_stg)) return false;
+      if (L == 0) {
+        for (int sb = 0; sb < kSB; ++sb) {
+          const int ci = r * kHB + sb % kHB;
+          const int x = 256 * (ci >> 2) + 128 * (sb / kHB) + 32 * (ci & 3);
+          ptx::tma_store_2d(map, stage_u32 + sb * kChunkBytes, x, y);
+        }
+        ptx::bulk_commit();
+        ptx::bulk_wait_read();
+      }
+      if (!wait_leader()) return false;
+    }
+    return true;
+  };
   auto write_out = [&](int bb, float scale) -> bool {
+    if (p.out_f32) return store_rows_f32(&p.tm_out, bb * kHeads + 64 * (int)rank, scale);
 #pragma unroll 1
     for (int r = 0; r < 4 / kHB; ++r) {
 #pragma unroll 1
@@ -780,7 +822,8 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
     const uint32_t npieces = (uint32_t)(pl - pf + 1);
     xl[L] = l;
     // a split sequence whose other pieces are all counted already is completed by this CTA
-    if (!pc.full && L == 0) *merge_flag = (ptx::ld_acquire_gpu(cnt) + 1u == npieces) ? 1u : 0u;
+    if (!pc.full && p.fuse_merge && L == 0)
+      *merge_flag = (ptx::ld_acquire_gpu(cnt) + 1u == npieces) ? 1u : 0u;
     if (!sync4(lx, n_lx)) return;
     const float ltot = l + xl[L ^ 64];
     const float inv = 1.f / ltot;
@@ -788,53 +831,31 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
     const int head = 64 * (int)rank + m;
     bool merge = false;
     if (!pc.full) {
-      merge = *merge_flag != 0u;
+      merge = p.fuse_merge && *merge_flag != 0u;
       if (!merge) {
         // Publish this piece (normalised O in fp32 and its LSE) for the CTA that
         // completes the sequence: the LSE combine of mla_decode.py:212-246, fused
         // into this kernel (no second launch; nobody waits on another CTA).
         const int slot = pair * p.maxp + piece;
         if (hf == 0) p.part_lse[(size_t)slot * kHeads + head] = lse;
-        // fp32 chunk ci = (nh, k) of a thread is dims 256 nh + 128 hf + 32 k
-#pragma unroll 1
-        for (int r = 0; r < 8 / kHB; ++r) {
-#pragma unroll 1
-          for (int i = 0; i < kHB; ++i) {
-            const int ci = r * kHB + i;
-            uint32_t o[32];
-            ptx::tmem_ld32(tmem + lane_off + kColO + 32 * ci, o);
-            ptx::tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * inv);
-            st_box_row(stage + (hf * kHB + i) * kChunkBytes, m, o);
-          }
-          ptx::fence_proxy_async_smem();
+        if (!store_rows_f32(&p.tm_part, slot * kHeads + 64 * (int)rank, inv)) return;
+        if (p.fuse_merge) {
+          // the LSE stores of every thread are ordered before the count below
+          __threadfence();
           if (!sync4(stg, n_stg)) return;
           if (L == 0) {
-            for (int sb = 0; sb < kSB; ++sb) {
-              const int ci = r * kHB + sb % kHB;
-              const int x = 256 * (ci >> 2) + 128 * (sb / kHB) + 32 * (ci & 3);
-              ptx::tma_store_2d(&p.tm_part, stage_u32 + sb * kChunkBytes, x, slot * kHeads + 64 * (int)rank);
-            }
-            ptx::bulk_commit();
-            ptx::bulk_wait_read();
+            ptx::bulk_wait();
+            ptx::fence_proxy_async_all();
+            __threadfence();
+            const uint32_t done = atomicAdd(cnt, 1u) + 1u;
+            const bool last = done == npieces;
+            if (last) atomicExch(cnt, 0u);   // ready for the next call
+            *merge_flag = last ? 1u : 0u;
           }
           if (!wait_leader()) return;
+          merge = *merge_flag != 0u;
         }
-        // the LSE stores of every thread are ordered before the count below
-        __threadfence();
-        if (!sync4(stg, n_stg)) return;
-        if (L == 0) {
-          ptx::bulk_wait();
-          ptx::fence_proxy_async_all();
-          __threadfence();
-          const uint32_t done = atomicAdd(cnt, 1u) + 1u;
-          const bool last = done == npieces;
-          if (last) atomicExch(cnt, 0u);   // ready for the next call
-          *merge_flag = last ? 1u : 0u;
-        }
-        if (!wait_leader()) return;
-        merge = *merge_flag != 0u;
+        // else: a combine launch after this kernel merges the sequence
       } else if (L == 0) {
         atomicExch(cnt, 0u);   // every other piece was counted: reset for the next call
       }
@@ -912,8 +933,9 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         }
         if (!write_out(pc.bb, 1.f)) return;
       } else {
-        // rare (a sequence split over three or more pairs): merge from global memory
-        T* orow = static_cast<T*>(p.out) + ((size_t)pc.bb * kHeads + head) * kDim;
+        // rare (the pair's range goes on: the shared memory is busy): merge from
+        // global memory, row by row in registers
+        const size_t orow = ((size_t)pc.bb * kHeads + head) * kDim;
 #pragma unroll 1
         for (int cc = 0; cc < 8; ++cc) {
           const int d0 = 256 * (cc >> 2) + 128 * hf + 32 * (cc & 3);
@@ -938,12 +960,18 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
               acc[4 * g + 3] = fmaf(w, x.w, acc[4 * g + 3]);
             }
           }
-          T* dst = orow + d0;
+          if (p.out_f32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow + d0);
 #pragma unroll
-          for (int g = 0; g < 4; ++g)
-            reinterpret_cast<uint4*>(dst)[g] =
-                make_uint4(pack2<T>(acc[8 * g], acc[8 * g + 1]), pack2<T>(acc[8 * g + 2], acc[8 * g + 3]),
-                           pack2<T>(acc[8 * g + 4], acc[8 * g + 5]), pack2<T>(acc[8 * g + 6], acc[8 * g + 7]));
+            for (int g = 0; g < 8; ++g)
+              dst[g] = make_float4(acc[4 * g], acc[4 * g + 1], acc[4 * g + 2], acc[4 * g + 3]);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + orow + d0);
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+              dst[g] = make_uint4(pack2<T>(acc[8 * g], acc[8 * g + 1]), pack2<T>(acc[8 * g + 2], acc[8 * g + 3]),
+                                  pack2<T>(acc[8 * g + 4], acc[8 * g + 5]), pack2<T>(acc[8 * g + 6], acc[8 * g + 7]));
+          }
         }
       }
       if (hf == 0 && p.lse_out != nullptr) p.lse_out[(size_t)pc.bb * kHeads + head] = big;
@@ -1076,6 +1104,69 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
 }
 
 // ---------------------------------------------------------------------------
+// combine launch for sequences split between many pairs (the kernel above ran
+// with fuse_merge = 0): one 128-thread CTA per (head, sequence), 4 columns per
+// thread; sequences one pair covered whole were written by that pair and are
+// skipped.  Same LSE algebra as mla_combine.cu (mla_decode.py:212-246).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void store4_out(float* dst, float4 v) { *reinterpret_cast<float4*>(dst) = v; }
+template <typename T>
+__device__ __forceinline__ void store4_out(T* dst, float4 v) {
+  *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<T>(v.x, v.y), pack2<T>(v.z, v.w));
+}
+
+template <typename OutT>
+__global__ void __launch_bounds__(128)
+mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__ part_o,
+                        OutT* __restrict__ out, float* __restrict__ lse_out, uint32_t total_tiles,
+                        int nt, int pairs, int maxp) {
+  __shared__ float s_lse[kMaxPairs];
+  __shared__ uint32_t s_slot[kMaxPairs];
+  const int head = blockIdx.x, bb = blockIdx.y, tid = threadIdx.x;
+  int pf, pl;
+  pairs_of_sequence(total_tiles, pairs, nt, bb, &pf, &pl);
+  if (pf == pl) return;
+  const int n = pl - pf + 1;
+  for (int k = tid; k < n; k += 128) {
+    const uint32_t sl = (uint32_t)pair_slot(pf + k, bb, total_tiles, pairs, nt, maxp);
+    s_slot[k] = sl;
+    s_lse[k] = __ldg(part_lse + (size_t)sl * kHeads + head);
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int k = 0; k < n; ++k) mx = fmaxf(mx, s_lse[k]);
+  float sum = 0.f;
+  for (int k = 0; k < n; ++k) sum += exp2f((s_lse[k] - mx) * kLog2e);
+  const float lse = mx + logf(sum);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  int k = 0;
+  for (; k + 4 <= n; k += 4) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      v[u] = __ldg(reinterpret_cast<const float4*>(part_o + ((size_t)s_slot[k + u] * kHeads + head) * kDim) + tid);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float w = exp2f((s_lse[k + u] - lse) * kLog2e);
+      acc.x = fmaf(w, v[u].x, acc.x);
+      acc.y = fmaf(w, v[u].y, acc.y);
+      acc.z = fmaf(w, v[u].z, acc.z);
+      acc.w = fmaf(w, v[u].w, acc.w);
+    }
+  }
+  for (; k < n; ++k) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(part_o + ((size_t)s_slot[k] * kHeads + head) * kDim) + tid);
+    const float w = exp2f((s_lse[k] - lse) * kLog2e);
+    acc.x = fmaf(w, v.x, acc.x);
+    acc.y = fmaf(w, v.y, acc.y);
+    acc.z = fmaf(w, v.z, acc.z);
+    acc.w = fmaf(w, v.w, acc.w);
+  }
+  store4_out(out + ((size_t)bb * kHeads + head) * kDim + 4 * tid, acc);
+  if (lse_out != nullptr && tid == 0) lse_out[(size_t)bb * kHeads + head] = lse;
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1189,14 +1280,26 @@ SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int
   pl.bpc = pairs;                // CTA pairs
   pl.extra = maxp;               // slots per pair
   pl.part_rows = (long long)pairs * maxp * sm100::kHeads;
-  // no combine launch when every pair's range starts on a sequence boundary
+  // partials exist unless every pair's range starts on a sequence boundary
   pl.needs_combine = false;
   for (int pp = 1; pp < pairs; ++pp)
     if (((long long)pp * total / pairs) % nt != 0) pl.needs_combine = true;
+  // Sequences split between a few pairs are merged inside the kernel by the last
+  // pair to finish; one split between many (long contexts, small batches) goes to
+  // a combine launch, which merges all heads in parallel instead of one pair
+  // reading every partial.
+  int most = 1;
+  for (int bb = 0; bb < batch && pl.needs_combine; ++bb) {
+    const long long x0 = (long long)bb * nt;
+    const long long pf = ((x0 + 1) * pairs + total - 1) / total - 1;
+    const long long pz = ((x0 + nt) * pairs + total - 1) / total - 1;
+    if (pz - pf + 1 > most) most = (int)(pz - pf + 1);
+  }
+  *variant = most > sm100::kFuseMaxPieces ? 1 : 0;
   return pl;
 }
 
-cudaError_t launch_sm100_decode(const DecodeArgs& a, int) {
+cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
   using namespace sm100;
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
@@ -1213,8 +1316,12 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int) {
   const uint64_t kv_rows = (uint64_t)a.batch * a.seqlen_kv;
   const uint64_t q_rows = (uint64_t)a.batch * kHeads;
   if (!make_map(&p.tm_kv, a.kv, kDim, kv_rows, dt) || !make_map(&p.tm_kpe, a.k_pe, kPeDim, kv_rows, dt) ||
-      !make_map(&p.tm_q, a.q, kDim, q_rows, dt) || !make_map(&p.tm_qpe, a.q_pe, kPeDim, q_rows, dt) ||
-      !make_map(&p.tm_out, a.out, kDim, q_rows, dt))
+      !make_map(&p.tm_q, a.q, kDim, q_rows, dt) || !make_map(&p.tm_qpe, a.q_pe, kPeDim, q_rows, dt))
+    return cudaErrorInvalidValue;
+  p.out_f32 = a.out_dtype == MLA_DTYPE_F32 ? 1 : 0;
+  p.fuse_merge = variant == 0 ? 1 : 0;
+  if (!(p.out_f32 ? make_map(&p.tm_out, a.out, kDim, q_rows, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4)
+                  : make_map(&p.tm_out, a.out, kDim, q_rows, dt)))
     return cudaErrorInvalidValue;
   if (a.part_o != nullptr &&
       !make_map(&p.tm_part, a.part_o, kDim, (uint64_t)a.plan.part_rows, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4))
@@ -1241,6 +1348,24 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int) {
         <<<2 * pairs, kThreads, Smem<__nv_bfloat16>::kBytes, a.stream>>>(p);
   else
     mla_sm100_decode_kernel<__half><<<2 * pairs, kThreads, Smem<__half>::kBytes, a.stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sm100_combine(const DecodeArgs& a) {
+  using namespace sm100;
+  const int nt = (a.seqlen_kv + kTile - 1) / kTile;
+  const uint32_t total = (uint32_t)a.batch * (uint32_t)nt;
+  const dim3 grid(kHeads, a.batch);
+  if (a.out_dtype == MLA_DTYPE_F32)
+    mla_pair_combine_kernel<float><<<grid, 128, 0, a.stream>>>(
+        a.part_lse, a.part_o, static_cast<float*>(a.out), a.lse, total, nt, a.plan.bpc, a.plan.extra);
+  else if (a.dtype == MLA_DTYPE_BF16)
+    mla_pair_combine_kernel<__nv_bfloat16><<<grid, 128, 0, a.stream>>>(
+        a.part_lse, a.part_o, static_cast<__nv_bfloat16*>(a.out), a.lse, total, nt, a.plan.bpc,
+        a.plan.extra);
+  else
+    mla_pair_combine_kernel<__half><<<grid, 128, 0, a.stream>>>(
+        a.part_lse, a.part_o, static_cast<__half*>(a.out), a.lse, total, nt, a.plan.bpc, a.plan.extra);
   return cudaGetLastError();
 }
 

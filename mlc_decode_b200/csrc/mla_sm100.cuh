@@ -14,4 +14,7 @@ SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int
 // Enqueue the tensor-core split-KV kernel; partials go to a.part_o/a.part_lse.
 cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant);
 
+// Enqueue the combine of split sequences for plans whose variant is 1 (no in-kernel merge).
+cudaError_t launch_sm100_combine(const DecodeArgs& a);
+
 }  // namespace mla

@@ -85,6 +85,30 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst_smem, const void* 
       : "memory");
 }
 
+// Same, with an L2 eviction-priority policy (see l2_policy_*).
+__device__ __forceinline__ void tma_load_2d_pair_hint(uint32_t dst_smem, const void* desc,
+                                                      uint32_t cluster_bar, int32_t x, int32_t y,
+                                                      uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst_smem),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(cluster_bar), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
+// L2 eviction-priority policies for cache-hinted loads: keep lines that are
+// read again soon, let lines read for the last time go first.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 // Per-warpgroup register budget (every warp of the warpgroup executes it).
 template <uint32_t kRegs>
 __device__ __forceinline__ void setmaxnreg_inc() {
@@ -139,6 +163,12 @@ __device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, ui
 __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),
                "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void prefetch_l2_hint(const void* src, uint32_t bytes, uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(src)),
+               "r"(bytes), "l"(policy)
                : "memory");
 }
 

@@ -109,6 +109,31 @@ class MlaDecodeKernel:
         capi.decode_fwd(q.data_ptr(), q_pe.data_ptr(), kv.data_ptr(), k_pe.data_ptr(), out.data_ptr(),
                         lse_ptr, ws.data_ptr(), ws.numel(), b, h, s, _DTYPES[dtype], self._ccfg, stream)
 
+    def partial(self, q, q_pe, kv, k_pe, o, lse):
+        """Decode against this KV part with a float32 result (mla_decode_partial).
+
+        ``o`` float32 [batch, heads, 512] receives the normalised output and
+        ``lse`` float32 [batch, heads] the natural-log log-sum-exp; results of
+        several parts of the same sequences merge with :func:`combine`.
+        """
+        b, h, s = self.batch, self.heads, self.seqlen_kv
+        dtype = q.dtype if isinstance(q, torch.Tensor) else None
+        if dtype not in _DTYPES:
+            raise ValueError(f"q must be float16 or bfloat16, got {dtype}")
+        dev = q.device
+        _check_tensor("q", q, (b, h, DIM), dtype, None)
+        _check_tensor("q_pe", q_pe, (b, h, PE_DIM), dtype, dev)
+        _check_tensor("kv", kv, (b, s, 1, DIM), dtype, dev)
+        _check_tensor("k_pe", k_pe, (b, s, 1, PE_DIM), dtype, dev)
+        _check_tensor("o", o, (b, h, DIM), torch.float32, dev)
+        _check_tensor("lse", lse, (b, h), torch.float32, dev)
+        ws = self._workspace(dev, dtype)
+        with torch.cuda.device(dev):
+            stream = torch.cuda.current_stream(dev).cuda_stream
+        capi.decode_partial(q.data_ptr(), q_pe.data_ptr(), kv.data_ptr(), k_pe.data_ptr(), o.data_ptr(),
+                            lse.data_ptr(), ws.data_ptr(), ws.numel(), b, h, s, _DTYPES[dtype],
+                            self._ccfg, stream)
+
     def splitkv(self, q, q_pe, kv, k_pe, out, lse=None):
         """First launch of a call only (the split-KV kernel); pair with ``combine_ws``.
 
@@ -160,13 +185,16 @@ class MlaDecodeKernel:
 def combine(part_lse: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor, lse=None):
     """LSE-merge ``num_split`` normalised partials (split-major) into ``out``.
 
-    part_lse float32 [ns, b, h] (natural log), part_o float32 [ns, b, h, 512].
+    part_lse float32 [ns, b, h] (natural log), part_o float32 [ns, b, h, 512];
+    ``out`` is float16, bfloat16 or float32 [b, h, 512].
     """
     ns, b, h = part_lse.shape
     _check_tensor("part_lse", part_lse, (ns, b, h), torch.float32, None)
     _check_tensor("part_o", part_o, (ns, b, h, DIM), torch.float32, part_lse.device)
-    if out.dtype not in _DTYPES:
-        raise ValueError("out must be float16 or bfloat16")
+    out_types = dict(_DTYPES)
+    out_types[torch.float32] = capi.MLA_DTYPE_F32
+    if out.dtype not in out_types:
+        raise ValueError("out must be float16, bfloat16 or float32")
     _check_tensor("out", out, (b, h, DIM), out.dtype, part_lse.device)
     lse_ptr = None
     if lse is not None:
@@ -175,4 +203,4 @@ def combine(part_lse: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor, lse
     with torch.cuda.device(part_lse.device):
         stream = torch.cuda.current_stream(part_lse.device).cuda_stream
     capi.combine(part_lse.data_ptr(), part_o.data_ptr(), ns, b, h, out.data_ptr(), lse_ptr,
-                 _DTYPES[out.dtype], stream)
+                 out_types[out.dtype], stream)

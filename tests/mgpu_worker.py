@@ -1,0 +1,65 @@
+"""Worker of tests/test_multi_gpu.py: one rank per GPU over NCCL.
+
+Checks, on every rank, (a) the batch split (this rank's block of sequences,
+no collective) and (b) the sequence split (this rank's part of every KV
+cache, float32 partials all-gathered and merged), both against the float64
+oracle.  Exits non-zero on a parity failure.
+"""
+import datetime
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from mlc_decode_b200 import MlaDecodeKernel  # noqa: E402
+from mlc_decode_b200.dist import SequenceSplitDecoder, batch_shard  # noqa: E402
+from oracle import mla_oracle as O  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", local))
+    ok = True
+    try:
+        dev = torch.device("cuda", local)
+        # (a) batch split
+        inputs = O.make_inputs(6, 128, 1000, "bf16", seed=71)
+        sl = batch_shard(6, rank, world)
+        mine = [t[sl].contiguous() for t in inputs]
+        q, qp, kv, kp = (t.to(dev) for t in mine)
+        out = torch.empty_like(q)
+        lse = torch.empty(q.shape[0], 128, device=dev)
+        MlaDecodeKernel(q.shape[0], 128, 1, 1000)(q, qp, kv, kp, out, lse)
+        torch.cuda.synchronize()
+        ref, rl = O.ref_program_f64(*mine)
+        res = O.check_parity(out.float().cpu().numpy(), lse.cpu().numpy(), ref, rl, "bf16")
+        print(f"rank {rank} batch split {res}", flush=True)
+        ok &= res["ok"]
+        # (b) sequence split
+        b, h, s = 1, 128, 20000
+        inputs = O.make_inputs(b, h, s, "bf16", seed=72)
+        dec = SequenceSplitDecoder(b, h, s)
+        q, qp = inputs[0].to(dev), inputs[1].to(dev)
+        kv = inputs[2][:, dec.start:dec.end].contiguous().to(dev)
+        kp = inputs[3][:, dec.start:dec.end].contiguous().to(dev)
+        out = torch.empty(b, h, 512, dtype=torch.bfloat16, device=dev)
+        lse = torch.empty(b, h, device=dev)
+        dec(q, qp, kv, kp, out, lse)
+        torch.cuda.synchronize()
+        ref, rl = O.ref_program_f64(*inputs)
+        res = O.check_parity(out.float().cpu().numpy(), lse.cpu().numpy(), ref, rl, "bf16")
+        print(f"rank {rank} sequence split rows [{dec.start}, {dec.end}) {res}", flush=True)
+        ok &= res["ok"]
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+    sys.exit(0 if ok else 1)
+
+
+if __name__ == "__main__":
+    main()

@@ -207,3 +207,91 @@ def test_combine_entry_point_merges_partials(cuda):
     ref, ref_lse = O.ref_program_f64(*inputs)
     res = O.check_parity(out.float().cpu().numpy(), big.cpu().numpy(), ref, ref_lse, "bf16")
     assert res["ok"], res
+
+
+def _f32_check(o, lse, ref, ref_lse):
+    """float32 results: no output rounding, so the gate is on the float64 oracle itself."""
+    assert not np.isnan(o).any() and not np.isnan(lse).any()
+    assert O.rel_l2(o, ref) <= O.REL_L2_TOL, O.rel_l2(o, ref)
+    assert np.abs(o - ref).max() <= O.MAX_ABS_TOL
+    assert np.abs(lse - ref_lse).max() <= O.LSE_TOL
+
+
+@pytest.mark.parametrize("cfg", [{}, {"kernel": "simt", "num_split": 1}, {"kernel": "simt", "num_split": 5}],
+                         ids=["auto", "simt-ns1", "simt-ns5"])
+@pytest.mark.parametrize("b,h,s,dtype", [(2, 128, 1000, "bf16"), (3, 128, 4096, "fp16"), (2, 64, 700, "bf16")])
+def test_partial_entry_point_float32(b, h, s, dtype, cfg, cuda):
+    """mla_decode_partial: float32 normalised O and LSE of a KV part."""
+    from mlc_decode_b200 import MlaDecodeKernel
+
+    inputs = O.make_inputs(b, h, s, dtype, seed=31)
+    q, q_pe, kv, k_pe = (t.cuda() for t in inputs)
+    k = MlaDecodeKernel(b, h, 1, s, cfg=cfg)
+    o = torch.full((b, h, 512), float("nan"), device="cuda")
+    lse = torch.full((b, h), float("nan"), device="cuda")
+    k.partial(q, q_pe, kv, k_pe, o, lse)
+    torch.cuda.synchronize()
+    ref, ref_lse = O.ref_program_f64(*inputs)
+    _f32_check(o.cpu().numpy(), lse.cpu().numpy(), ref, ref_lse)
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_sequence_split_emulated_on_one_gpu(world, cuda):
+    """The cross-GPU sequence split, its ranks run one after another on one GPU:
+    seq_shard parts -> mla_decode_partial each -> stacked -> mla_combine."""
+    from mlc_decode_b200 import MlaDecodeKernel, combine
+    from mlc_decode_b200.dist import seq_shard
+
+    b, h, s = 2, 128, 5000
+    inputs = O.make_inputs(b, h, s, "bf16", seed=41)
+    q, q_pe, kv, k_pe = (t.cuda() for t in inputs)
+    o_all = torch.zeros(world, b, h, 512, device="cuda")
+    l_all = torch.full((world, b, h), float("-inf"), device="cuda")
+    for r in range(world):
+        t0, t1 = seq_shard(s, r, world)
+        if t1 > t0:
+            MlaDecodeKernel(b, h, 1, t1 - t0).partial(q, q_pe, kv[:, t0:t1].contiguous(),
+                                                      k_pe[:, t0:t1].contiguous(), o_all[r], l_all[r])
+    out = torch.empty(b, h, 512, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(b, h, device="cuda")
+    combine(l_all, o_all, out, lse)
+    torch.cuda.synchronize()
+    ref, ref_lse = O.ref_program_f64(*inputs)
+    res = O.check_parity(out.float().cpu().numpy(), lse.cpu().numpy(), ref, ref_lse, "bf16")
+    assert res["ok"], res
+
+
+@pytest.mark.parametrize("b,s", [(1, 32768), (2, 20000)])
+def test_many_piece_sequences_use_the_combine_launch(b, s, cuda):
+    """A sequence split between many CTA pairs is merged by a second launch."""
+    from mlc_decode_b200 import MlaDecodeKernel
+
+    k = MlaDecodeKernel(b, 128, 1, s)
+    plan = k.plan(torch.bfloat16)
+    assert plan["kernel"] == "tc" and plan["launches"] == 2, plan
+    inputs = O.make_inputs(b, 128, s, "bf16", seed=51)
+    out, lse = run_decode(inputs)
+    ref, ref_lse = O.ref_program_f64(*inputs)
+    res = O.check_parity(out, lse, ref, ref_lse, "bf16")
+    assert res["ok"], res
+    # and the float32 variant through the same launches
+    q, q_pe, kv, k_pe = (t.cuda() for t in inputs)
+    o = torch.empty(b, 128, 512, device="cuda")
+    l32 = torch.empty(b, 128, device="cuda")
+    k.partial(q, q_pe, kv, k_pe, o, l32)
+    torch.cuda.synchronize()
+    _f32_check(o.cpu().numpy(), l32.cpu().numpy(), ref, ref_lse)
+
+
+def test_combine_float32_output(cuda):
+    """mla_combine with a float32 out (a result that can be combined again)."""
+    from mlc_decode_b200 import combine
+
+    inputs = O.make_inputs(1, 128, 900, "fp16", seed=61)
+    o, lse = O.splitkv_partials_f64(*inputs, [(0, 300), (300, 900)])
+    out = torch.empty(1, 128, 512, dtype=torch.float32, device="cuda")
+    big = torch.empty(1, 128, dtype=torch.float32, device="cuda")
+    combine(torch.from_numpy(lse).float().cuda(), torch.from_numpy(o).float().cuda(), out, big)
+    torch.cuda.synchronize()
+    ref, ref_lse = O.ref_program_f64(*inputs)
+    _f32_check(out.cpu().numpy(), big.cpu().numpy(), ref, ref_lse)
