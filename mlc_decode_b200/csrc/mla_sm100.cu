@@ -71,7 +71,6 @@ constexpr uint32_t kRegsLow = 88, kRegsSoftmax = 232;
 static_assert(2 * 128 * kRegsLow + 128 * kRegsSoftmax <= 384 * 168, "register split");
 constexpr float kRescaleLog2 = 8.0f;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
-constexpr int kPrefetchTiles = 2;
 constexpr int kMaxPairs = 256;        // CTA pairs per launch (schedule bound)
 constexpr int kFuseMaxPieces = 3;     // most pieces of one sequence merged in-kernel
 // A merge stages another pair's 64 partial rows (fp32, 2 KB each) in shared memory
@@ -234,21 +233,6 @@ struct Ring {
   }
 };
 
-// Pull this CTA's 64 rows of flattened tile `t` (latent 64 KB, rope 8 KB, both
-// contiguous) into L2, so that the TMA loads of that tile later hit L2: this keeps
-// enough bytes in flight to HBM without spending shared memory on deeper rings.
-__device__ __forceinline__ void prefetch_tile(const Params& p, uint32_t t, uint32_t rank,
-                                              uint64_t keep) {
-  const int bb = (int)(t / (uint32_t)p.nt);
-  const int jj = (int)(t - (uint32_t)bb * (uint32_t)p.nt);
-  const long long row0 = (long long)bb * p.seqlen + (long long)jj * kTile + 64 * (int)rank;
-  const long long rows = (long long)bb * p.seqlen + p.seqlen - row0;
-  if (rows <= 0) return;
-  const uint32_t n = rows < 64 ? (uint32_t)rows : 64u;
-  ptx::prefetch_l2_hint(p.kv + row0 * (kDim * 2), n * (kDim * 2), keep);   // read by K and V
-  ptx::prefetch_l2(p.kpe + row0 * (kPeDim * 2), n * (kPeDim * 2));
-}
-
 // ---------------------------------------------------------------------------
 // K producer: Q once per piece, then per tile 4 latent units + 1 rope unit.
 // ---------------------------------------------------------------------------
@@ -265,20 +249,16 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
   PieceIter it(p, pair);
   // the first Q rows are requested before any K or V traffic
   if (!wait_bar(c, ptx::smem_u32(&bars->q_go), 0u, kErrKLoad)) return;
-  const uint32_t t_end = it.t1;
-  uint32_t t_cur = it.t;
-  // (tile 0 is loaded at once; its prefetch would only add requests)
-  // latent rows are read twice (K now, V one tile later): keep them in L2;
-  // rope rows are read once
+  // Latent rows are read twice (K now, V one tile later): keep them in L2;
+  // rope rows are read once.  (No bulk L2 prefetch ahead of the ring: on B200
+  // it measured ~6 % slower at the bench shape.)
   const uint64_t keep = ptx::l2_policy_evict_last();
   const uint64_t once = ptx::l2_policy_evict_first();
-  for (int d = 1; d < kPrefetchTiles && t_cur + d < t_end; ++d) prefetch_tile(p, t_cur + d, rank, keep);
   Piece pc;
   // K units stream straight across piece boundaries: Q has its own loader thread
   while (it.next(&pc)) {
 #pragma unroll 1
-    for (int j = pc.first; j < pc.end; ++j, ++t_cur) {
-      if (t_cur + kPrefetchTiles < t_end) prefetch_tile(p, t_cur + kPrefetchTiles, rank, keep);
+    for (int j = pc.first; j < pc.end; ++j) {
       const int y = pc.bb * p.seqlen + j * kTile + 64 * (int)rank;
 #pragma unroll 1
       for (int u = 0; u < 5; ++u) {
