@@ -103,7 +103,8 @@ int resolve(int batch, int heads, int seqlen_kv, const MlaCfg* cfg, Resolved* r)
 }
 
 // Workspace layout:
-//   tensor-core kernel: [status word, 256 B][piece counters uint32 x batch x 2, padded to 256 B]
+//   tensor-core kernel: [status word, 256 B][piece counters uint32 x batch x ceil(heads/128) x 2,
+//                       padded to 256 B]
 //                       [partial LSE float32 x rows, padded to 256 B][partial O float32 x rows x 512]
 //                       (partials only when some sequence is split between CTA pairs)
 //   CUDA-core kernel:   [partial LSE][partial O] when the plan has more than one split
@@ -111,14 +112,17 @@ int resolve(int batch, int heads, int seqlen_kv, const MlaCfg* cfg, Resolved* r)
 // workspace); every call leaves them zero again.
 constexpr size_t kStatusBytes = 256;
 
-size_t counter_bytes(int batch) { return align_up((size_t)batch * 2 * sizeof(uint32_t), 256); }
+// one counter per (sequence, group of 128 heads, CTA rank) of the tensor-core kernel
+size_t counter_bytes(int batch, int heads) {
+  return align_up((size_t)batch * head_groups(heads) * 2 * sizeof(uint32_t), 256);
+}
 
 size_t part_rows(int batch, int heads, const Resolved& r) {
   return r.plan.part_rows > 0 ? (size_t)r.plan.part_rows : (size_t)r.plan.ns * batch * heads;
 }
 
 size_t workspace_for(int batch, int heads, const Resolved& r) {
-  const size_t head = r.kernel == MLA_KERNEL_TC ? kStatusBytes + counter_bytes(batch) : 0;
+  const size_t head = r.kernel == MLA_KERNEL_TC ? kStatusBytes + counter_bytes(batch, heads) : 0;
   if (!r.plan.needs_combine) return head;
   const size_t rows = part_rows(batch, heads, r);
   return head + align_up(rows * sizeof(float), 256) + rows * kDim * sizeof(float);
@@ -163,7 +167,7 @@ int32_t mla_describe_plan(int32_t batch, int32_t heads, int32_t seqlen_kv, int32
   out4[0] = r.kernel;
   out4[1] = tc ? r.plan.bpc : r.plan.ns;
   out4[2] = (r.plan.needs_combine && (!tc || r.tc_variant == 1)) ? 2 : 1;
-  out4[3] = tc ? (int64_t)(kStatusBytes + counter_bytes(batch)) : 0;
+  out4[3] = tc ? (int64_t)(kStatusBytes + counter_bytes(batch, heads)) : 0;
   return MLA_OK;
 }
 
@@ -232,7 +236,7 @@ int prepare(const char* fn, const void* q, const void* q_pe, const void* kv, con
     if (r->kernel == MLA_KERNEL_TC) {
       a->status = reinterpret_cast<uint32_t*>(base);
       a->counters = reinterpret_cast<uint32_t*>(base + kStatusBytes);
-      base += kStatusBytes + counter_bytes(batch);
+      base += kStatusBytes + counter_bytes(batch, heads);
     }
     if (r->plan.needs_combine) {
       const size_t rows = part_rows(batch, heads, *r);

@@ -134,9 +134,9 @@ struct Smem {
 struct Params {
   CUtensorMap tm_kv;    // [b*s, 512], box 64 x 64
   CUtensorMap tm_kpe;   // [b*s, 64]
-  CUtensorMap tm_q;     // [b*128, 512]
-  CUtensorMap tm_qpe;   // [b*128, 64]
-  CUtensorMap tm_out;   // [b*128, 512] output rows, box 64 x 64 (stores)
+  CUtensorMap tm_q;     // [b][h][512], box 64 x 64 x 1 (rows past h read as zero)
+  CUtensorMap tm_qpe;   // [b][h][64]
+  CUtensorMap tm_out;   // [b][h][512] output rows, box 64 x 64 x 1 (stores; rows past h not written)
   CUtensorMap tm_part;  // [slots*128, 512] float32 partial rows, box 32 x 64 (stores)
   const uint8_t* kv;    // raw rows, for L2 prefetch
   const uint8_t* kpe;
@@ -148,8 +148,11 @@ struct Params {
   float* part_lse;
   uint32_t* status;
   uint32_t* counters;   // [batch][2] pieces finished per (sequence, CTA rank); zero between calls
+  // Work units are "virtual sequences": sequence s, head group g (heads
+  // [128 g, 128 g + 128)) is v = s * hgroups + g; batch counts them.
   uint32_t total_tiles;  // batch x tiles per sequence; total_tiles * (pairs + 1) < 2^32
   int batch, seqlen, nt, pairs, maxp;
+  int heads, hgroups;   // real head count; head groups of 128 per sequence
   int out_f32;          // `out` is float32 (tm_out then has 32 x 64 float boxes)
   int fuse_merge;       // merge split sequences here (last arriver); else a combine launch does
   float sl2;            // softmax scale * log2(e)
@@ -192,7 +195,13 @@ __device__ __forceinline__ bool aborted(const Ctx& c) {
   return *reinterpret_cast<volatile uint32_t*>(c.abort_local) != 0u;
 }
 
-// One contiguous run of tiles of one sequence inside a pair's range.
+// Sequence and first head row (within the sequence) of virtual sequence v.
+__device__ __forceinline__ int vseq_seq(const Params& p, int v) { return p.hgroups == 1 ? v : v / p.hgroups; }
+__device__ __forceinline__ int vseq_head0(const Params& p, int v) {
+  return p.hgroups == 1 ? 0 : (v % p.hgroups) * kHeads;
+}
+
+// One contiguous run of tiles of one (virtual) sequence inside a pair's range.
 struct Piece {
   int bb;        // sequence
   int first;     // first tile (within the sequence)
@@ -259,7 +268,7 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
   while (it.next(&pc)) {
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j) {
-      const int y = pc.bb * p.seqlen + j * kTile + 64 * (int)rank;
+      const int y = vseq_seq(p, pc.bb) * p.seqlen + j * kTile + 64 * (int)rank;
 #pragma unroll 1
       for (int u = 0; u < 5; ++u) {
         if (!wait_bar(c, kempty0 + 8 * ring.stage, ring.phase ^ 1u, kErrKLoad)) return;
@@ -279,11 +288,14 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
   }
 }
 
-// Pull this CTA's 64 Q rows of sequence `bb` (latent 64 KB, rope 8 KB) into L2.
-__device__ __forceinline__ void prefetch_q(const Params& p, int bb, uint32_t rank) {
-  const long long row0 = (long long)bb * kHeads + 64 * (int)rank;
-  ptx::prefetch_l2(p.q + row0 * (kDim * 2), 64 * (kDim * 2));
-  ptx::prefetch_l2(p.qpe + row0 * (kPeDim * 2), 64 * (kPeDim * 2));
+// Pull this CTA's (up to) 64 Q rows of virtual sequence `v` into L2.
+__device__ __forceinline__ void prefetch_q(const Params& p, int v, uint32_t rank) {
+  const int h0 = vseq_head0(p, v) + 64 * (int)rank;
+  const int rows = p.heads - h0 < 64 ? p.heads - h0 : 64;
+  if (rows <= 0) return;
+  const long long row0 = (long long)vseq_seq(p, v) * p.heads + h0;
+  ptx::prefetch_l2(p.q + row0 * (kDim * 2), (uint32_t)rows * (kDim * 2));
+  ptx::prefetch_l2(p.qpe + row0 * (kPeDim * 2), (uint32_t)rows * (kPeDim * 2));
 }
 
 // ---------------------------------------------------------------------------
@@ -317,21 +329,22 @@ __device__ __forceinline__ void q_loader(const Params& p, const Ctx& c, uint32_t
     Piece nxt;
     if (peek.next(&nxt)) prefetch_q(p, nxt.bb, rank);
     if (piece > 0 && !wait_bar(c, q_empty, (uint32_t)(piece - 1) & 1u, kErrKLoad)) return;
-    const int qrow = pc.bb * kHeads + 64 * (int)rank;
+    const int qseq = vseq_seq(p, pc.bb);
+    const int qrow = vseq_head0(p, pc.bb) + 64 * (int)rank;   // head row within the sequence
     // the first piece stages dims [0, 256) in the (still unused) P buffers and loads
     // everything at once; later pieces reuse the Q region once the TMEM copy is made
     const uint32_t qt_dst = sbase + (piece == 0 ? S::kP : S::kQ);
     ptx::mbar_arrive_expect_tx(qts, 4 * kChunkBytes);
 #pragma unroll 1
     for (int ch = 0; ch < 4; ++ch)
-      ptx::tma_load_2d_local(qt_dst + ch * kChunkBytes, &p.tm_q, qts, 64 * ch, qrow);
+      ptx::tma_load_3d_local(qt_dst + ch * kChunkBytes, &p.tm_q, qts, 64 * ch, qrow, qseq);
     if (piece > 0 && !wait_bar(c, qtr, (uint32_t)piece & 1u, kErrKLoad)) return;
     if (leader) ptx::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
 #pragma unroll 1
     for (int ch = 0; ch < 4; ++ch)
-      ptx::tma_load_2d_pair(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, q_full_leader, kQTDims + 64 * ch,
-                            qrow);
-    ptx::tma_load_2d_pair(sbase + S::kQ + 4 * kChunkBytes, &p.tm_qpe, q_full_leader, 0, qrow);
+      ptx::tma_load_3d_pair(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, q_full_leader, kQTDims + 64 * ch,
+                            qrow, qseq);
+    ptx::tma_load_3d_pair(sbase + S::kQ + 4 * kChunkBytes, &p.tm_qpe, q_full_leader, 0, qrow, qseq);
     if (piece == 0) ptx::mbar_arrive_local(q_go);
     ++piece;
   }
@@ -358,7 +371,7 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
   while (it.next(&pc)) {
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j) {
-      const int y0 = pc.bb * p.seqlen + j * kTile;
+      const int y0 = vseq_seq(p, pc.bb) * p.seqlen + j * kTile;
 #pragma unroll 1
       for (int u = 0; u < 4; ++u) {
         const int nh = u >> 1, th = u & 1;
@@ -623,7 +636,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
   // stage O (TMEM) x scale as float32 rows and store them with TMA to rows
   // [y, y + 64) of `map`; fp32 chunk ci = (nh, k) of a thread is dims
   // 256 nh + 128 hf + 32 k
-  auto store_rows_f32 = [&](const CUtensorMap* map, int y, float scale) -> bool {
+  auto store_rows_f32 = [&](const CUtensorMap* map, int y, int z, float scale) -> bool {
 #pragma unroll 1
     for (int r = 0; r < 8 / kHB; ++r) {
 #pragma unroll 1
@@ -642,7 +655,10 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         for (int sb = 0; sb < kSB; ++sb) {
           const int ci = r * kHB + sb % kHB;
           const int x = 256 * (ci >> 2) + 128 * (sb / kHB) + 32 * (ci & 3);
-          ptx::tma_store_2d(map, stage_u32 + sb * kChunkBytes, x, y);
+          if (z < 0)
+            ptx::tma_store_2d(map, stage_u32 + sb * kChunkBytes, x, y);
+          else
+            ptx::tma_store_3d(map, stage_u32 + sb * kChunkBytes, x, y, z);
         }
         ptx::bulk_commit();
         ptx::bulk_wait_read();
@@ -652,7 +668,8 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
     return true;
   };
   auto write_out = [&](int bb, float scale) -> bool {
-    if (p.out_f32) return store_rows_f32(&p.tm_out, bb * kHeads + 64 * (int)rank, scale);
+    const int oseq = vseq_seq(p, bb), orow = vseq_head0(p, bb) + 64 * (int)rank;
+    if (p.out_f32) return store_rows_f32(&p.tm_out, orow, oseq, scale);
 #pragma unroll 1
     for (int r = 0; r < 4 / kHB; ++r) {
 #pragma unroll 1
@@ -675,7 +692,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         for (int sb = 0; sb < kSB; ++sb) {
           const int co = r * kHB + sb % kHB;
           const int x = 256 * (co >> 1) + 128 * (sb / kHB) + 64 * (co & 1);
-          ptx::tma_store_2d(&p.tm_out, stage_u32 + sb * kChunkBytes, x, bb * kHeads + 64 * (int)rank);
+          ptx::tma_store_3d(&p.tm_out, stage_u32 + sb * kChunkBytes, x, orow, oseq);
         }
         ptx::bulk_commit();
         ptx::bulk_wait_read();
@@ -808,7 +825,10 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
     const float ltot = l + xl[L ^ 64];
     const float inv = 1.f / ltot;
     const float lse = (m_run * sl2 + log2f(ltot)) * kLn2;
-    const int head = 64 * (int)rank + m;
+    const int head = 64 * (int)rank + m;                   // row within the head group
+    const int hglob = vseq_head0(p, pc.bb) + head;         // head within the sequence
+    const size_t orow_g = (size_t)vseq_seq(p, pc.bb) * p.heads + hglob;
+    const bool real = hglob < p.heads;
     bool merge = false;
     if (!pc.full) {
       merge = p.fuse_merge && *merge_flag != 0u;
@@ -818,7 +838,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         // into this kernel (no second launch; nobody waits on another CTA).
         const int slot = pair * p.maxp + piece;
         if (hf == 0) p.part_lse[(size_t)slot * kHeads + head] = lse;
-        if (!store_rows_f32(&p.tm_part, slot * kHeads + 64 * (int)rank, inv)) return;
+        if (!store_rows_f32(&p.tm_part, slot * kHeads + 64 * (int)rank, -1, inv)) return;
         if (p.fuse_merge) {
           // the LSE stores of every thread are ordered before the count below
           __threadfence();
@@ -843,7 +863,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
     if (!merge) {
       if (pc.full) {
         if (!write_out(pc.bb, inv)) return;
-        if (hf == 0 && p.lse_out != nullptr) p.lse_out[(size_t)pc.bb * kHeads + head] = lse;
+        if (hf == 0 && real && p.lse_out != nullptr) p.lse_out[orow_g] = lse;
       }
     } else {
       // this CTA completes a split sequence: merge every piece into `out`
@@ -915,7 +935,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
       } else {
         // rare (the pair's range goes on: the shared memory is busy): merge from
         // global memory, row by row in registers
-        const size_t orow = ((size_t)pc.bb * kHeads + head) * kDim;
+        const size_t orow = orow_g * kDim;
 #pragma unroll 1
         for (int cc = 0; cc < 8; ++cc) {
           const int d0 = 256 * (cc >> 2) + 128 * hf + 32 * (cc & 3);
@@ -940,7 +960,9 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
               acc[4 * g + 3] = fmaf(w, x.w, acc[4 * g + 3]);
             }
           }
-          if (p.out_f32) {
+          if (!real) {
+            // a head past h in the last head group: computed, not stored
+          } else if (p.out_f32) {
             float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow + d0);
 #pragma unroll
             for (int g = 0; g < 8; ++g)
@@ -954,7 +976,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
           }
         }
       }
-      if (hf == 0 && p.lse_out != nullptr) p.lse_out[(size_t)pc.bb * kHeads + head] = big;
+      if (hf == 0 && real && p.lse_out != nullptr) p.lse_out[orow_g] = big;
     }
     ptx::tc_fence_before();
     __syncwarp();
@@ -1099,7 +1121,7 @@ template <typename OutT>
 __global__ void __launch_bounds__(128)
 mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__ part_o,
                         OutT* __restrict__ out, float* __restrict__ lse_out, uint32_t total_tiles,
-                        int nt, int pairs, int maxp) {
+                        int nt, int pairs, int maxp, int heads, int hgroups) {
   __shared__ float s_lse[kMaxPairs];
   __shared__ uint32_t s_slot[kMaxPairs];
   const int head = blockIdx.x, bb = blockIdx.y, tid = threadIdx.x;
@@ -1142,8 +1164,11 @@ mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restr
     acc.z = fmaf(w, v.z, acc.z);
     acc.w = fmaf(w, v.w, acc.w);
   }
-  store4_out(out + ((size_t)bb * kHeads + head) * kDim + 4 * tid, acc);
-  if (lse_out != nullptr && tid == 0) lse_out[(size_t)bb * kHeads + head] = lse;
+  const int hglob = (bb % hgroups) * kHeads + head;
+  if (hglob >= heads) return;   // a head past h in the last head group
+  const size_t orow = (size_t)(bb / hgroups) * heads + hglob;
+  store4_out(out + orow * kDim + 4 * tid, acc);
+  if (lse_out != nullptr && tid == 0) lse_out[orow] = lse;
 }
 
 // ---------------------------------------------------------------------------
@@ -1173,6 +1198,21 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, CU
   const cuuint32_t box[2] = {128 / elem_bytes, 64};
   const cuuint32_t estr[2] = {1, 1};
   return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 3D row-major [depth, rows, cols] tensor (batch, heads, dims), boxes of 64 rows x
+// 128 bytes x 1, 128-byte swizzle.
+bool make_map3(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t depth,
+               CUtensorMapDataType dt, uint32_t elem_bytes = 2) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[3] = {cols, rows, depth};
+  const cuuint64_t strides[2] = {cols * elem_bytes, rows * cols * elem_bytes};
+  const cuuint32_t box[3] = {128 / elem_bytes, 64, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -1233,16 +1273,19 @@ int current_max_pairs() {
 
 }  // namespace sm100
 
+int head_groups(int heads) { return (heads + sm100::kHeads - 1) / sm100::kHeads; }
+
 bool sm100_supports(int batch, int heads, int seqlen_kv) {
   // 32-bit tile arithmetic in the kernel and int32 TMA row coordinates
+  if (heads < 1 || seqlen_kv < 1 || batch < 1) return false;
   const long long nt = (seqlen_kv + sm100::kTile - 1) / sm100::kTile;
-  return heads == sm100::kHeads && seqlen_kv >= 1 && batch >= 1 &&
-         (long long)batch * nt * (sm100::kMaxPairs + 1) < (1ll << 32) &&
+  const long long vb = (long long)batch * head_groups(heads);
+  return vb * nt * (sm100::kMaxPairs + 1) < (1ll << 32) &&
          (long long)batch * seqlen_kv < (1ll << 31) - sm100::kTile;
 }
 
 SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int* variant) {
-  (void)heads;
+  batch *= head_groups(heads);   // virtual sequences: one per (sequence, group of 128 heads)
   SplitPlan pl{};
   *variant = 0;
   pl.block_n = sm100::kTile;
@@ -1294,14 +1337,14 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
   const CUtensorMapDataType dt =
       a.dtype == MLA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const uint64_t kv_rows = (uint64_t)a.batch * a.seqlen_kv;
-  const uint64_t q_rows = (uint64_t)a.batch * kHeads;
   if (!make_map(&p.tm_kv, a.kv, kDim, kv_rows, dt) || !make_map(&p.tm_kpe, a.k_pe, kPeDim, kv_rows, dt) ||
-      !make_map(&p.tm_q, a.q, kDim, q_rows, dt) || !make_map(&p.tm_qpe, a.q_pe, kPeDim, q_rows, dt))
+      !make_map3(&p.tm_q, a.q, kDim, a.heads, a.batch, dt) ||
+      !make_map3(&p.tm_qpe, a.q_pe, kPeDim, a.heads, a.batch, dt))
     return cudaErrorInvalidValue;
   p.out_f32 = a.out_dtype == MLA_DTYPE_F32 ? 1 : 0;
   p.fuse_merge = variant == 0 ? 1 : 0;
-  if (!(p.out_f32 ? make_map(&p.tm_out, a.out, kDim, q_rows, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4)
-                  : make_map(&p.tm_out, a.out, kDim, q_rows, dt)))
+  if (!(p.out_f32 ? make_map3(&p.tm_out, a.out, kDim, a.heads, a.batch, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4)
+                  : make_map3(&p.tm_out, a.out, kDim, a.heads, a.batch, dt)))
     return cudaErrorInvalidValue;
   if (a.part_o != nullptr &&
       !make_map(&p.tm_part, a.part_o, kDim, (uint64_t)a.plan.part_rows, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4))
@@ -1316,10 +1359,12 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
   p.part_lse = a.part_lse;
   p.status = a.status;
   p.counters = a.counters;
-  p.batch = a.batch;
+  p.heads = a.heads;
+  p.hgroups = head_groups(a.heads);
+  p.batch = a.batch * p.hgroups;
   p.seqlen = a.seqlen_kv;
   p.nt = (a.seqlen_kv + kTile - 1) / kTile;
-  p.total_tiles = (uint32_t)a.batch * (uint32_t)p.nt;
+  p.total_tiles = (uint32_t)p.batch * (uint32_t)p.nt;
   p.pairs = pairs;
   p.maxp = a.plan.extra;
   p.sl2 = a.softmax_scale * kLog2e;
@@ -1334,18 +1379,22 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
 cudaError_t launch_sm100_combine(const DecodeArgs& a) {
   using namespace sm100;
   const int nt = (a.seqlen_kv + kTile - 1) / kTile;
-  const uint32_t total = (uint32_t)a.batch * (uint32_t)nt;
-  const dim3 grid(kHeads, a.batch);
+  const int hg = head_groups(a.heads);
+  const int vb = a.batch * hg;
+  const uint32_t total = (uint32_t)vb * (uint32_t)nt;
+  const dim3 grid(kHeads, vb);
   if (a.out_dtype == MLA_DTYPE_F32)
     mla_pair_combine_kernel<float><<<grid, 128, 0, a.stream>>>(
-        a.part_lse, a.part_o, static_cast<float*>(a.out), a.lse, total, nt, a.plan.bpc, a.plan.extra);
+        a.part_lse, a.part_o, static_cast<float*>(a.out), a.lse, total, nt, a.plan.bpc, a.plan.extra, a.heads,
+        hg);
   else if (a.dtype == MLA_DTYPE_BF16)
     mla_pair_combine_kernel<__nv_bfloat16><<<grid, 128, 0, a.stream>>>(
         a.part_lse, a.part_o, static_cast<__nv_bfloat16*>(a.out), a.lse, total, nt, a.plan.bpc,
-        a.plan.extra);
+        a.plan.extra, a.heads, hg);
   else
     mla_pair_combine_kernel<__half><<<grid, 128, 0, a.stream>>>(
-        a.part_lse, a.part_o, static_cast<__half*>(a.out), a.lse, total, nt, a.plan.bpc, a.plan.extra);
+        a.part_lse, a.part_o, static_cast<__half*>(a.out), a.lse, total, nt, a.plan.bpc, a.plan.extra,
+        a.heads, hg);
   return cudaGetLastError();
 }
 

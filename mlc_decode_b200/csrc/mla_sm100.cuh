@@ -5,6 +5,9 @@
 
 namespace mla {
 
+// Groups of 128 heads per sequence: the tensor-core kernel's work units.
+int head_groups(int heads);
+
 // True when the tensor-core kernel covers this shape.
 bool sm100_supports(int batch, int heads, int seqlen_kv);
 

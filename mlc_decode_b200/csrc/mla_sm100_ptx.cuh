@@ -109,6 +109,32 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   return p;
 }
 
+// 3D tiled forms (coordinates x innermost): pair load, local load, store.
+// Out-of-range box elements read as zero and are not written.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst_smem, const void* desc, uint32_t cluster_bar,
+                                                 int32_t x, int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst_smem),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(cluster_bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_local(uint32_t dst_smem, const void* desc, uint32_t bar, int32_t x,
+                                                  int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst_smem),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const void* desc, uint32_t src_smem, int32_t x, int32_t y,
+                                             int32_t z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(src_smem), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
 // Per-warpgroup register budget (every warp of the warpgroup executes it).
 template <uint32_t kRegs>
 __device__ __forceinline__ void setmaxnreg_inc() {

@@ -3,7 +3,8 @@
 The reference derives all of this for a 104-AP MetaX C500 with 64 KB of
 shared memory (mla_decode.py:504-606).  The B200 numbers differ: 148 SMs,
 up to 227 KB of shared memory per CTA, and two decode kernels (the tcgen05
-tensor-core kernel for 128-head groups, the CUDA-core kernel for the rest).
+tensor-core kernel, which takes any head count as groups of 128 heads, and
+the CUDA-core kernel, used when a config asks for it).
 The config-dict contract is the reference's (mla_decode.py:588-598):
 block_N, block_H, num_split, spread, combine_groups, num_stages,
 dim_chunk_num, q_in_reg, threads; plus ``kernel`` ("tc"/"simt") here.
@@ -26,7 +27,7 @@ TABLE_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "mla_best_
 SIMT_BLOCK_H = 16
 SIMT_TILE = 32
 SIMT_CTAS_PER_SM = 2
-# Tensor-core kernel: a CTA pair owns 128 heads of one sequence; 128-row tiles.
+# Tensor-core kernel: a CTA pair owns a group of (up to) 128 heads of one sequence; 128-row tiles.
 TC_HEADS = 128
 TC_TILE = 128
 

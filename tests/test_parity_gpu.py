@@ -295,3 +295,18 @@ def test_combine_float32_output(cuda):
     torch.cuda.synchronize()
     ref, ref_lse = O.ref_program_f64(*inputs)
     _f32_check(out.cpu().numpy(), big.cpu().numpy(), ref, ref_lse)
+
+
+@pytest.mark.parametrize("h,dtype", [(16, "bf16"), (48, "fp16"), (100, "bf16"), (200, "bf16"), (256, "fp16")])
+def test_tensor_core_kernel_any_head_count(h, dtype, cuda):
+    """Head counts other than 128 run on the tensor-core kernel as groups of 128 heads
+    (rows past h read as zero and are never stored)."""
+    from mlc_decode_b200 import MlaDecodeKernel
+
+    b, s = 3, 1500
+    assert MlaDecodeKernel(b, h, 1, s).plan(TDT[dtype])["kernel"] == "tc"
+    inputs = O.make_inputs(b, h, s, dtype, seed=81)
+    out, lse = run_decode(inputs, {"kernel": "tc"})
+    ref, ref_lse = O.ref_program_f64(*inputs)
+    res = O.check_parity(out, lse, ref, ref_lse, dtype)
+    assert res["ok"], res
