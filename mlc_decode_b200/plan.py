@@ -104,4 +104,4 @@ def lookup(batch, heads, seqlen_kv, dtype_name, n_gpu=1, path=TABLE_PATH):
     ent = load_table(path).get(table_key(batch, heads, seqlen_kv, dtype_name, n_gpu))
     if ent is None:
         return None
-    return {k: v for k, v in ent.items() if k != "latency_us"}
+    return {k: v for k, v in ent.items() if k not in ("latency_us", "default_us")}
