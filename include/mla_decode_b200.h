@@ -177,6 +177,40 @@ int32_t mla_decode_partial(const void* q, const void* q_pe, const void* kv,
                            int32_t dtype, const MlaCfg* cfg, void* stream);
 
 /*
+ * Decode over KV caches of different lengths, optionally paged (the caller-side
+ * format of serving decode).  No counterpart in the reference, whose kernel takes
+ * one kv_ctx for the whole batch (its design notes name per-sequence lengths as
+ * the next step: docs/num_split_design.md).
+ *   cache_seqlens [batch] int32: KV rows of each sequence, clamped to
+ *                 [0, max_seqlen_kv]; a sequence with 0 rows gets out = 0 and
+ *                 lse = -inf.
+ *   block_table   NULL: kv_cache [batch, max_seqlen_kv, 1, 512] and k_pe_cache
+ *                 [batch, max_seqlen_kv, 1, 64], as mla_decode_fwd's kv/k_pe;
+ *                 else int32 [batch, max_pages_per_seq] page ids into
+ *                 kv_cache [num_pages, page_size, 1, 512] and
+ *                 k_pe_cache [num_pages, page_size, 1, 64]; row r of sequence b
+ *                 is row r % page_size of page block_table[b][r / page_size].
+ *                 page_size is a multiple of 64 and
+ *                 max_pages_per_seq x page_size >= max_seqlen_kv; entries past a
+ *                 sequence's length are not read.
+ * q, q_pe, out, lse, dtype and cfg as in mla_decode_fwd (tensor-core kernel only;
+ * cfg->num_split = CTA pairs).  `workspace` holds mla_paged_workspace_bytes()
+ * bytes, 256-byte aligned, zero before the first call (every call leaves its
+ * counters zero).  Three launches: the plan kernel (tile prefix sums from
+ * cache_seqlens, on the device: no host sync), the decode kernel, the combine.
+ */
+size_t mla_paged_workspace_bytes(int32_t batch, int32_t heads, int32_t max_seqlen_kv,
+                                 int32_t dtype, const MlaCfg* cfg);
+int32_t mla_decode_paged(const void* q, const void* q_pe, const void* kv_cache,
+                         const void* k_pe_cache, const int32_t* block_table,
+                         const int32_t* cache_seqlens, void* out, float* lse,
+                         void* workspace, size_t workspace_bytes,
+                         int32_t batch, int32_t heads, int32_t max_seqlen_kv,
+                         int32_t page_size, int32_t num_pages,
+                         int32_t max_pages_per_seq, int32_t dtype,
+                         const MlaCfg* cfg, void* stream);
+
+/*
  * mla_decode_fwd without a workspace argument, for callers that cannot
  * allocate device memory where they decode (code running under CUDA-graph
  * capture, servers that reserve all memory up front and forbid allocation on

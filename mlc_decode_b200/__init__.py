@@ -5,6 +5,6 @@ repository root; this package holds the C-ABI binding (``capi``), the kernel
 object (``decode``), the planner/config table (``plan``) and the multi-GPU
 partitioning (``dist``).
 """
-from .decode import MlaDecodeKernel, combine  # noqa: F401
+from .decode import MlaDecodeKernel, MlaPagedDecodeKernel, combine  # noqa: F401
 
-__all__ = ["MlaDecodeKernel", "combine"]
+__all__ = ["MlaDecodeKernel", "MlaPagedDecodeKernel", "combine"]

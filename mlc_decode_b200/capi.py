@@ -25,7 +25,8 @@ STATUS_NAMES = {0: "MLA_OK", 1: "MLA_ERR_ARG", 2: "MLA_ERR_WORKSPACE", 3: "MLA_E
 EXPORTED_SYMBOLS = ("mla_abi_version", "mla_last_error", "mla_split_plan",
                     "mla_workspace_bytes", "mla_decode_fwd", "mla_decode_splitkv",
                     "mla_decode_combine_ws", "mla_combine", "mla_decode_fwd_noalloc",
-                    "mla_describe_plan", "mla_decode_partial")
+                    "mla_describe_plan", "mla_decode_partial", "mla_paged_workspace_bytes",
+                    "mla_decode_paged")
 
 
 class MlaCfg(ctypes.Structure):
@@ -85,6 +86,11 @@ def load(build_if_missing: bool = True):
         lib.mla_decode_splitkv.restype = i32
         lib.mla_decode_partial.argtypes = lib.mla_decode_fwd.argtypes
         lib.mla_decode_partial.restype = i32
+        lib.mla_paged_workspace_bytes.argtypes = [i32, i32, i32, i32, ctypes.POINTER(MlaCfg)]
+        lib.mla_paged_workspace_bytes.restype = sz
+        lib.mla_decode_paged.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, sz, i32, i32, i32, i32, i32, i32,
+                                         i32, ctypes.POINTER(MlaCfg), vp]
+        lib.mla_decode_paged.restype = i32
         lib.mla_decode_combine_ws.argtypes = [vp, vp, vp, sz, i32, i32, i32, i32,
                                               ctypes.POINTER(MlaCfg), vp]
         lib.mla_decode_combine_ws.restype = i32
@@ -172,6 +178,24 @@ def decode_partial(q, q_pe, kv, k_pe, o, lse, ws, ws_bytes, batch, heads, seqlen
     """mla_decode_partial: float32 normalised O and natural-log LSE of this KV part."""
     check(load().mla_decode_partial(q, q_pe, kv, k_pe, o, lse, ws, ws_bytes, int(batch), int(heads),
                                     int(seqlen_kv), int(dtype), ctypes.byref(cfg), stream))
+
+
+def paged_workspace_bytes(batch, heads, max_seqlen_kv, dtype, cfg: MlaCfg) -> int:
+    lib = load()
+    n = lib.mla_paged_workspace_bytes(int(batch), int(heads), int(max_seqlen_kv), int(dtype), ctypes.byref(cfg))
+    if n == 0:
+        msg = last_error()
+        if msg:
+            raise MlaError(1, msg)
+    return int(n)
+
+
+def decode_paged(q, q_pe, kv_cache, k_pe_cache, block_table, cache_seqlens, out, lse, ws, ws_bytes, batch,
+                 heads, max_seqlen_kv, page_size, num_pages, max_pages, dtype, cfg: MlaCfg, stream) -> None:
+    """mla_decode_paged: per-sequence KV lengths, optional page table (pointers are device addresses)."""
+    check(load().mla_decode_paged(q, q_pe, kv_cache, k_pe_cache, block_table, cache_seqlens, out, lse, ws,
+                                  ws_bytes, int(batch), int(heads), int(max_seqlen_kv), int(page_size),
+                                  int(num_pages), int(max_pages), int(dtype), ctypes.byref(cfg), stream))
 
 
 def decode_splitkv(q, q_pe, kv, k_pe, out, lse, ws, ws_bytes, batch, heads, seqlen_kv, dtype,

@@ -368,3 +368,128 @@ int32_t mla_combine(const float* part_lse, const float* part_o, int32_t num_spli
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Ragged / paged decode (per-sequence KV lengths, optional page table).
+// Workspace: [status 256 B][counters u32 x batch x groups x 2, padded][tile prefix
+// sums u32 x (batch x groups + 1), padded][partial LSE][partial O].
+// ---------------------------------------------------------------------------
+namespace mla {
+namespace {
+
+struct PagedLayout {
+  SplitPlan plan;
+  size_t counters_off, cu_off, lse_off, o_off, total;
+};
+
+int paged_layout(int batch, int heads, int max_seqlen_kv, int dtype, const MlaCfg* cfg, PagedLayout* L) {
+  int rc = check_shape(batch, heads, max_seqlen_kv, dtype);
+  if (rc != MLA_OK) return rc;
+  MlaCfg c{};
+  if (cfg != nullptr) c = *cfg;
+  if (c.kernel == MLA_KERNEL_SIMT) {
+    set_error("mla_decode_paged: runs on the tensor-core kernel only (kernel = auto or tc)");
+    return MLA_ERR_UNSUPPORTED;
+  }
+  if (!sm100_supports(batch, heads, max_seqlen_kv)) {
+    set_error("mla_decode_paged: shape outside the tensor-core kernel (batch %d, heads %d, max_seqlen_kv %d)",
+              batch, heads, max_seqlen_kv);
+    return MLA_ERR_UNSUPPORTED;
+  }
+  L->plan = sm100_plan_ragged(batch, heads, max_seqlen_kv, c);
+  const size_t vb = (size_t)batch * head_groups(heads);
+  const size_t rows = (size_t)L->plan.part_rows;
+  L->counters_off = kStatusBytes;
+  L->cu_off = L->counters_off + counter_bytes(batch, heads);
+  L->lse_off = L->cu_off + align_up((vb + 1) * sizeof(uint32_t), 256);
+  L->o_off = L->lse_off + align_up(rows * sizeof(float), 256);
+  L->total = L->o_off + rows * kDim * sizeof(float);
+  return MLA_OK;
+}
+
+}  // namespace
+}  // namespace mla
+
+extern "C" {
+
+size_t mla_paged_workspace_bytes(int32_t batch, int32_t heads, int32_t max_seqlen_kv, int32_t dtype,
+                                 const MlaCfg* cfg) {
+  g_last_error.clear();
+  PagedLayout L;
+  if (paged_layout(batch, heads, max_seqlen_kv, dtype, cfg, &L) != MLA_OK) return 0;
+  return L.total;
+}
+
+int32_t mla_decode_paged(const void* q, const void* q_pe, const void* kv_cache, const void* k_pe_cache,
+                         const int32_t* block_table, const int32_t* cache_seqlens, void* out, float* lse,
+                         void* workspace, size_t workspace_bytes, int32_t batch, int32_t heads,
+                         int32_t max_seqlen_kv, int32_t page_size, int32_t num_pages,
+                         int32_t max_pages_per_seq, int32_t dtype, const MlaCfg* cfg, void* stream) {
+  const char* fn = "mla_decode_paged";
+  PagedLayout L;
+  int rc = paged_layout(batch, heads, max_seqlen_kv, dtype, cfg, &L);
+  if (rc != MLA_OK) return rc;
+  if (!q || !q_pe || !kv_cache || !k_pe_cache || !cache_seqlens || !out) {
+    set_error("%s: null pointer", fn);
+    return MLA_ERR_ARG;
+  }
+  if (!aligned16(q) || !aligned16(q_pe) || !aligned16(kv_cache) || !aligned16(k_pe_cache) || !aligned16(out)) {
+    set_error("%s: tensor pointers must be 16-byte aligned", fn);
+    return MLA_ERR_ARG;
+  }
+  if (block_table != nullptr) {
+    if (page_size < 64 || page_size % 64 != 0 || num_pages < 1 || max_pages_per_seq < 1 ||
+        (long long)max_pages_per_seq * page_size < max_seqlen_kv ||
+        (long long)num_pages * page_size >= (1ll << 31) - 256) {
+      set_error("%s: page_size must be a multiple of 64 and max_pages_per_seq x page_size >= max_seqlen_kv "
+                "(page_size %d, num_pages %d, max_pages_per_seq %d, max_seqlen_kv %d)",
+                fn, page_size, num_pages, max_pages_per_seq, max_seqlen_kv);
+      return MLA_ERR_ARG;
+    }
+  }
+  if (workspace == nullptr || workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) {
+    set_error("%s: workspace needs %zu bytes, 256-byte aligned (got %zu at %p)", fn, L.total, workspace_bytes,
+              workspace);
+    return MLA_ERR_WORKSPACE;
+  }
+  DecodeArgs a{};
+  a.q = q;
+  a.q_pe = q_pe;
+  a.kv = kv_cache;
+  a.k_pe = k_pe_cache;
+  a.out = out;
+  a.out_dtype = dtype;
+  a.lse = lse;
+  a.batch = batch;
+  a.heads = heads;
+  a.seqlen_kv = max_seqlen_kv;
+  a.dtype = dtype;
+  a.softmax_scale = (cfg != nullptr && cfg->softmax_scale != 0.f) ? cfg->softmax_scale : 1.0f / sqrtf((float)kQkDim);
+  if (!(a.softmax_scale > 0.f) || !isfinite(a.softmax_scale)) {
+    set_error("%s: softmax_scale must be finite and > 0", fn);
+    return MLA_ERR_ARG;
+  }
+  a.plan = L.plan;
+  a.stream = static_cast<cudaStream_t>(stream);
+  char* base = static_cast<char*>(workspace);
+  a.status = reinterpret_cast<uint32_t*>(base);
+  a.counters = reinterpret_cast<uint32_t*>(base + L.counters_off);
+  a.cu_tiles = reinterpret_cast<uint32_t*>(base + L.cu_off);
+  a.part_lse = reinterpret_cast<float*>(base + L.lse_off);
+  a.part_o = reinterpret_cast<float*>(base + L.o_off);
+  a.seqlens = cache_seqlens;
+  a.block_table = block_table;
+  a.page_size = block_table != nullptr ? page_size : 0;
+  a.num_pages = block_table != nullptr ? num_pages : 0;
+  a.max_pages = block_table != nullptr ? max_pages_per_seq : 0;
+  cudaError_t err = launch_sm100_ragged_plan(a);
+  if (err == cudaSuccess) err = launch_sm100_decode(a, 1);
+  if (err == cudaSuccess) err = launch_sm100_combine(a);
+  if (err != cudaSuccess) {
+    set_error("%s: launch failed: %s", fn, cudaGetErrorString(err));
+    return MLA_ERR_CUDA;
+  }
+  return MLA_OK;
+}
+
+}  // extern "C"

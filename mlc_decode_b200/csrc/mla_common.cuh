@@ -116,6 +116,11 @@ struct DecodeArgs {
   float* part_lse;    // [ns, batch, heads]
   uint32_t* status;   // workspace status word (tensor-core kernel), nullable
   uint32_t* counters; // per-(sequence, CTA rank) piece counters (tensor-core kernel)
+  // ragged calls (mla_decode_paged): per-sequence lengths, optional page table
+  const int* seqlens;      // [batch] or nullptr
+  const int* block_table;  // [batch][max_pages] or nullptr (contiguous [batch, seqlen_kv] rows)
+  int page_size, num_pages, max_pages;
+  uint32_t* cu_tiles;      // workspace: flattened-tile prefix sums (batch x head groups + 1)
   int batch, heads, seqlen_kv, dtype;
   float softmax_scale;  // multiplies raw scores
   SplitPlan plan;

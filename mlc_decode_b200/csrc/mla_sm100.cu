@@ -155,7 +155,14 @@ struct Params {
   int batch, seqlen, nt, pairs, maxp;
   int heads, hgroups;   // real head count; head groups of 128 per sequence
   int out_f32;          // `out` is float32 (tm_out then has 32 x 64 float boxes)
-  int fuse_merge;       // merge split sequences here (last arriver); else a combine launch does
+  int fuse_max;         // sequences split into at most this many pieces are merged here
+  // Ragged calls (per-sequence lengths, optionally paged KV): cu_tiles[v] is the
+  // first tile of virtual sequence v in the flattened list (batch + 1 entries,
+  // written by the plan kernel); nullptr for fixed-length calls.
+  const uint32_t* cu_tiles;
+  const int* seqlens;      // [real batch] KV rows per sequence, or nullptr (all seqlen)
+  const int* block_table;  // [real batch][max_pages] page ids, or nullptr (contiguous rows)
+  int page_size, max_pages;
   float sl2;            // softmax scale * log2(e)
 };
 
@@ -210,26 +217,93 @@ struct Piece {
   bool full;     // the run is the whole sequence
 };
 
-// Iterates the pieces of pair `pair`'s tile range [pair*T/P, (pair+1)*T/P)
-// (32-bit arithmetic: the host keeps T * (P + 1) below 2^32).
+// The flattened tile list: virtual sequence v owns tiles [first(v), first(v+1)).
+// Fixed-length calls: first(v) = v * nt; ragged calls: the prefix sums cu_tiles.
+// Pair pp owns [pp*T/P, (pp+1)*T/P) (32-bit arithmetic: the host keeps
+// T * (P + 1) below 2^32).
+struct TileMap {
+  const uint32_t* cu;
+  uint32_t nt, total, pairs;
+  int batch;
+  __device__ __forceinline__ uint32_t first(int v) const {
+    return cu != nullptr ? __ldg(cu + v) : (uint32_t)v * nt;
+  }
+  __device__ __forceinline__ uint32_t range_start(int pp) const { return (uint32_t)pp * total / pairs; }
+  // pair whose range holds tile x
+  __device__ __forceinline__ int pair_of(uint32_t x) const {
+    return (int)(((x + 1) * pairs + total - 1) / total) - 1;
+  }
+  // sequence holding tile x (x < total): the last v with first(v) <= x
+  __device__ int seq_of(uint32_t x) const {
+    if (cu == nullptr) return (int)(x / nt);
+    int lo = 0, hi = batch - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (first(mid) <= x) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  }
+};
+
+// Pairs that own tiles: a ragged call may launch more pairs than it has tiles;
+// the extra pairs own empty ranges past the end, never one inside a sequence.
+__device__ __forceinline__ uint32_t effective_pairs(uint32_t launched, uint32_t total) {
+  const uint32_t pp = launched < total ? launched : total;
+  return pp > 0 ? pp : 1u;
+}
+
+__device__ __forceinline__ TileMap tile_map(const Params& p) {
+  TileMap m;
+  m.cu = p.cu_tiles;
+  m.nt = (uint32_t)p.nt;
+  m.batch = p.batch;
+  m.total = p.cu_tiles != nullptr ? __ldg(p.cu_tiles + p.batch) : p.total_tiles;
+  m.pairs = effective_pairs((uint32_t)p.pairs, m.total);
+  return m;
+}
+
+// Iterates the pieces of pair `pair`'s tile range; empty sequences are skipped.
 struct PieceIter {
-  uint32_t t, t1, nt;
-  __device__ PieceIter(const Params& p, int pair) : nt((uint32_t)p.nt) {
-    t = (uint32_t)pair * p.total_tiles / (uint32_t)p.pairs;
-    t1 = (uint32_t)(pair + 1) * p.total_tiles / (uint32_t)p.pairs;
+  TileMap m;
+  uint32_t t, t1;
+  int v;
+  __device__ PieceIter(const Params& p, int pair) : m(tile_map(p)) {
+    if ((uint32_t)pair < m.pairs) {
+      t = m.range_start(pair);
+      t1 = m.range_start(pair + 1);
+    } else {
+      t = t1 = m.total;   // a pair past the ones that own tiles
+    }
+    v = t < t1 ? m.seq_of(t) : 0;
   }
   __device__ bool next(Piece* pc) {
     if (t >= t1) return false;
-    pc->bb = (int)(t / nt);
-    const uint32_t bstart = (uint32_t)pc->bb * nt;
-    const uint32_t e = t1 < bstart + nt ? t1 : bstart + nt;
+    while (m.first(v + 1) <= t) ++v;
+    const uint32_t bstart = m.first(v), bend = m.first(v + 1);
+    const uint32_t e = t1 < bend ? t1 : bend;
+    pc->bb = v;
     pc->first = (int)(t - bstart);
     pc->end = (int)(e - bstart);
-    pc->full = pc->first == 0 && pc->end == nt;
+    pc->full = t == bstart && e == bend;
     t = e;
     return true;
   }
 };
+
+// KV rows of virtual sequence v, and the row in the KV tensor map of row `row`
+// of sequence `seq` (contiguous [b, seqlen] rows, or a page of block_table).
+__device__ __forceinline__ int seq_len(const Params& p, int v) {
+  if (p.seqlens == nullptr) return p.seqlen;
+  const int len = __ldg(p.seqlens + vseq_seq(p, v));   // clamped to [0, seqlen]: see the plan kernel
+  return len < 0 ? 0 : (len > p.seqlen ? p.seqlen : len);
+}
+__device__ __forceinline__ int kv_row(const Params& p, int seq, int row, int len) {
+  if (p.block_table == nullptr) return seq * p.seqlen + row;
+  // rows past the sequence's end are masked: read page 0 rather than a table entry
+  // the caller may not have filled
+  const int pg = row < len ? __ldg(p.block_table + (size_t)seq * p.max_pages + row / p.page_size) : 0;
+  return pg * p.page_size + row % p.page_size;
+}
 
 // Position in a ring of `kStages` shared-memory stages.
 template <int kStages>
@@ -269,7 +343,7 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
   while (it.next(&pc)) {
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j) {
-      const int y = vseq_seq(p, pc.bb) * p.seqlen + j * kTile + 64 * (int)rank;
+      const int y = kv_row(p, vseq_seq(p, pc.bb), j * kTile + 64 * (int)rank, seq_len(p, pc.bb));
 #pragma unroll 1
       for (int u = 0; u < 5; ++u) {
         if (!wait_bar(c, kempty0 + 8 * ring.stage, ring.phase ^ 1u, kErrKLoad)) return;
@@ -372,7 +446,7 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
   while (it.next(&pc)) {
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j) {
-      const int y0 = vseq_seq(p, pc.bb) * p.seqlen + j * kTile;
+      const int vseq = vseq_seq(p, pc.bb), vlen = seq_len(p, pc.bb);
 #pragma unroll 1
       for (int u = 0; u < 4; ++u) {
         const int nh = u >> 1, th = u & 1;
@@ -382,8 +456,9 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
         const uint32_t bar = vfull0_leader + 8 * ring.stage;
         const int x = 256 * nh + 128 * (int)rank;
         // the latent rows' last read
-        ptx::tma_load_2d_pair_hint(dst, &p.tm_kv, bar, x, y0 + 64 * th, once);
-        ptx::tma_load_2d_pair_hint(dst + kChunkBytes, &p.tm_kv, bar, x + 64, y0 + 64 * th, once);
+        const int yv = kv_row(p, vseq, j * kTile + 64 * th, vlen);
+        ptx::tma_load_2d_pair_hint(dst, &p.tm_kv, bar, x, yv, once);
+        ptx::tma_load_2d_pair_hint(dst + kChunkBytes, &p.tm_kv, bar, x + 64, yv, once);
         ring.advance();
       }
     }
@@ -525,18 +600,17 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Workspace slot of sequence bb's piece inside pair pp's range.
-__device__ __forceinline__ size_t pair_slot(int pp, int bb, uint32_t total_tiles, int pairs, int nt,
-                                            int maxp) {
-  return (size_t)pp * maxp + (bb - (int)((uint32_t)pp * total_tiles / (uint32_t)pairs / (uint32_t)nt));
+// Workspace slot of sequence bb's piece inside pair pp's range: two per pair,
+// 0 for the piece the range starts in, 1 for the piece it ends in (only a
+// range's first and last pieces can be parts of a split sequence).
+__device__ __forceinline__ size_t pair_slot(const TileMap& m, int pp, int bb) {
+  return (size_t)pp * 2 + (m.first(bb) <= m.range_start(pp) ? 0 : 1);
 }
 
-// First and last pair whose tile range [p*T/P, (p+1)*T/P) meets sequence bb.
-__device__ __forceinline__ void pairs_of_sequence(uint32_t total_tiles, int pairs, int nt, int bb,
-                                                  int* pf, int* pl) {
-  const uint32_t x0 = (uint32_t)bb * (uint32_t)nt;
-  *pf = (int)(((x0 + 1) * (uint32_t)pairs + total_tiles - 1) / total_tiles) - 1;
-  *pl = (int)(((x0 + (uint32_t)nt) * (uint32_t)pairs + total_tiles - 1) / total_tiles) - 1;
+// First and last pair whose tile range meets (non-empty) sequence bb.
+__device__ __forceinline__ void pairs_of_sequence(const TileMap& m, int bb, int* pf, int* pl) {
+  *pf = m.pair_of(m.first(bb));
+  *pl = m.pair_of(m.first(bb + 1) - 1);
 }
 
 // Copy this CTA's staged Q rows, latent dims [0, 256) (four SW128 boxes at
@@ -704,6 +778,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
   };
 
   PieceIter it(p, pair);
+  const TileMap& tm = it.m;
   Piece pc;
   int piece = 0;
   bool have = it.next(&pc);
@@ -712,6 +787,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
     PieceIter peek = it;
     Piece nxt;
     const bool has_next = peek.next(&nxt);
+    const int slen = seq_len(p, pc.bb);
     float m_run = -INFINITY, l = 0.f;
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j, ++gi) {
@@ -732,7 +808,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         v[k] = __uint_as_float(r0[k]);
         v[32 + k] = __uint_as_float(r1[k]);
       }
-      const int nvalid = p.seqlen - (j * kTile + 64 * hf);
+      const int nvalid = slen - (j * kTile + 64 * hf);
       if (nvalid < 64) {
 #pragma unroll
         for (int k = 0; k < 64; ++k)
@@ -815,12 +891,14 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
     if (!wait_bar(c, o_done0 + 8 * ((gi - 1) & 1u), ((gi - 1) >> 1) & 1u, kErrSoftmax)) return;
     ptx::tc_fence_after();
     int pf = 0, pl = 0;
-    if (!pc.full) pairs_of_sequence(p.total_tiles, p.pairs, p.nt, pc.bb, &pf, &pl);
+    if (!pc.full) pairs_of_sequence(tm, pc.bb, &pf, &pl);
     uint32_t* cnt = p.counters + 2 * pc.bb + rank;
     const uint32_t npieces = (uint32_t)(pl - pf + 1);
+    // sequences split between more pairs are left to the combine launch
+    const bool fuse = npieces <= (uint32_t)p.fuse_max;
     xl[L] = l;
     // a split sequence whose other pieces are all counted already is completed by this CTA
-    if (!pc.full && p.fuse_merge && L == 0)
+    if (!pc.full && fuse && L == 0)
       *merge_flag = (ptx::ld_acquire_gpu(cnt) + 1u == npieces) ? 1u : 0u;
     if (!sync4(lx, n_lx)) return;
     const float ltot = l + xl[L ^ 64];
@@ -832,15 +910,15 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
     const bool real = hglob < p.heads;
     bool merge = false;
     if (!pc.full) {
-      merge = p.fuse_merge && *merge_flag != 0u;
+      merge = fuse && *merge_flag != 0u;
       if (!merge) {
         // Publish this piece (normalised O in fp32 and its LSE) for the CTA that
         // completes the sequence: the LSE combine of mla_decode.py:212-246, fused
         // into this kernel (no second launch; nobody waits on another CTA).
-        const int slot = pair * p.maxp + piece;
+        const int slot = 2 * pair + (piece == 0 ? 0 : 1);
         if (hf == 0) p.part_lse[(size_t)slot * kHeads + head] = lse;
         if (!store_rows_f32(&p.tm_part, slot * kHeads + 64 * (int)rank, -1, inv)) return;
-        if (p.fuse_merge) {
+        if (fuse) {
           // the LSE stores of every thread are ordered before the count below
           __threadfence();
           if (!sync4(stg, n_stg)) return;
@@ -873,12 +951,12 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
       float mx = lse;
       for (int pp = pf; pp <= pl; ++pp)
         if (pp != own)
-          mx = fmaxf(mx, __ldcg(p.part_lse + pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp) *
+          mx = fmaxf(mx, __ldcg(p.part_lse + pair_slot(tm, pp, pc.bb) *
                                                 kHeads + head));
       float sum = exp2f((lse - mx) * kLog2e);
       for (int pp = pf; pp <= pl; ++pp)
         if (pp != own)
-          sum += exp2f((__ldcg(p.part_lse + pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp) *
+          sum += exp2f((__ldcg(p.part_lse + pair_slot(tm, pp, pc.bb) *
                                                kHeads + head) - mx) * kLog2e);
       const float big = mx + logf(sum);
       if (!has_next) {
@@ -900,7 +978,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         const uint32_t mstage = ptx::smem_u32(smem);
         for (int pp = pf; pp <= pl; ++pp) {
           if (pp == own) continue;
-          const size_t sl = pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp);
+          const size_t sl = pair_slot(tm, pp, pc.bb);
           const float w = exp2f((__ldcg(p.part_lse + sl * kHeads + head) - big) * kLog2e);
           if (L == 0) {
             ptx::fence_proxy_async_all();
@@ -949,7 +1027,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
           for (int k = 0; k < 32; ++k) acc[k] = __uint_as_float(o[k]) * w_own;
           for (int pp = pf; pp <= pl; ++pp) {
             if (pp == own) continue;
-            const size_t sl = pair_slot(pp, pc.bb, p.total_tiles, p.pairs, p.nt, p.maxp);
+            const size_t sl = pair_slot(tm, pp, pc.bb);
             const float w = exp2f((__ldcg(p.part_lse + sl * kHeads + head) - big) * kLog2e);
             const float4* src = reinterpret_cast<const float4*>(p.part_o + (sl * kHeads + head) * kDim + d0);
 #pragma unroll
@@ -1107,10 +1185,10 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
 }
 
 // ---------------------------------------------------------------------------
-// combine launch for sequences split between many pairs (the kernel above ran
-// with fuse_merge = 0): one 128-thread CTA per (head, sequence), 4 columns per
-// thread; sequences one pair covered whole were written by that pair and are
-// skipped.  Same LSE algebra as mla_combine.cu (mla_decode.py:212-246).
+// combine launch for sequences split between more pairs than the kernel above
+// merges itself (fuse_max): one 128-thread CTA per (head, sequence), 4 columns per
+// thread; other sequences were written by the decode kernel and are skipped.
+// Same LSE algebra as mla_combine.cu (mla_decode.py:212-246).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void store4_out(float* dst, float4 v) { *reinterpret_cast<float4*>(dst) = v; }
 template <typename T>
@@ -1121,17 +1199,25 @@ __device__ __forceinline__ void store4_out(T* dst, float4 v) {
 template <typename OutT>
 __global__ void __launch_bounds__(128)
 mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__ part_o,
-                        OutT* __restrict__ out, float* __restrict__ lse_out, uint32_t total_tiles,
-                        int nt, int pairs, int maxp, int heads, int hgroups) {
+                        OutT* __restrict__ out, float* __restrict__ lse_out, const uint32_t* cu,
+                        uint32_t total_fixed, int nt, int pairs, int vbatch, int heads, int hgroups,
+                        int fuse_max) {
   __shared__ float s_lse[kMaxPairs];
   __shared__ uint32_t s_slot[kMaxPairs];
   const int head = blockIdx.x, bb = blockIdx.y, tid = threadIdx.x;
+  TileMap m;
+  m.cu = cu;
+  m.nt = (uint32_t)nt;
+  m.batch = vbatch;
+  m.total = cu != nullptr ? __ldg(cu + vbatch) : total_fixed;
+  m.pairs = effective_pairs((uint32_t)pairs, m.total);
+  if (m.first(bb) == m.first(bb + 1)) return;   // empty sequence (written by the plan kernel)
   int pf, pl;
-  pairs_of_sequence(total_tiles, pairs, nt, bb, &pf, &pl);
-  if (pf == pl) return;
+  pairs_of_sequence(m, bb, &pf, &pl);
   const int n = pl - pf + 1;
+  if (n <= fuse_max) return;   // whole, or merged by the decode kernel
   for (int k = tid; k < n; k += 128) {
-    const uint32_t sl = (uint32_t)pair_slot(pf + k, bb, total_tiles, pairs, nt, maxp);
+    const uint32_t sl = (uint32_t)pair_slot(m, pf + k, bb);
     s_slot[k] = sl;
     s_lse[k] = __ldg(part_lse + (size_t)sl * kHeads + head);
   }
@@ -1170,6 +1256,50 @@ mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restr
   const size_t orow = (size_t)(bb / hgroups) * heads + hglob;
   store4_out(out + orow * kDim + 4 * tid, acc);
   if (lse_out != nullptr && tid == 0) lse_out[orow] = lse;
+}
+
+// ---------------------------------------------------------------------------
+// Plan of a ragged call (per-sequence KV lengths), one CTA: cu[v] = first tile of
+// virtual sequence v (batch x head groups + 1 entries) over lengths clamped to
+// [0, max_len]; sequences with no KV rows get out = 0 and lse = -inf here (the
+// decode kernel never visits them).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024)
+mla_ragged_plan_kernel(const int* __restrict__ seqlens, int batch, int heads, int hgroups, int max_len,
+                       uint32_t* __restrict__ cu, void* __restrict__ out, float* __restrict__ lse,
+                       int out_elem_bytes) {
+  __shared__ uint32_t s_part[1024];
+  const int tid = threadIdx.x;
+  const int vb = batch * hgroups;
+  auto tiles = [&](int v) -> uint32_t {
+    int len = seqlens[v / hgroups];
+    len = len < 0 ? 0 : (len > max_len ? max_len : len);
+    return (uint32_t)((len + kTile - 1) / kTile);
+  };
+  const int per = (vb + 1023) / 1024;
+  const int v0 = tid * per, v1 = v0 + per < vb ? v0 + per : vb;
+  uint32_t sum = 0;
+  for (int v = v0; v < v1; ++v) sum += tiles(v);
+  s_part[tid] = sum;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {   // inclusive scan of the chunk sums
+    const uint32_t x = tid >= off ? s_part[tid - off] : 0u;
+    __syncthreads();
+    s_part[tid] += x;
+    __syncthreads();
+  }
+  uint32_t run = tid > 0 ? s_part[tid - 1] : 0u;
+  for (int v = v0; v < v1; ++v) {
+    cu[v] = run;
+    run += tiles(v);
+  }
+  if (tid == 1023) cu[vb] = s_part[1023];
+  for (int row = tid; row < batch * heads; row += 1024) {
+    if (seqlens[row / heads] > 0) continue;
+    uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(out) + (size_t)row * kDim * out_elem_bytes);
+    for (int i = 0; i < kDim * out_elem_bytes / 16; ++i) o[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (lse != nullptr) lse[row] = -INFINITY;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1308,8 +1438,7 @@ SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int
       pairs = (int)whole;
   }
   if ((long long)pairs > total) pairs = (int)total;
-  const long long per = (total + pairs - 1) / pairs;
-  const int maxp = (int)((per + nt - 1) / nt) + 1;
+  const int maxp = 2;            // partial slots per pair: its first and its last piece
   pl.ns = pairs * maxp;          // partial slots
   pl.bpc = pairs;                // CTA pairs
   pl.extra = maxp;               // slots per pair
@@ -1347,13 +1476,15 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
   Params p{};
   const CUtensorMapDataType dt =
       a.dtype == MLA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const uint64_t kv_rows = (uint64_t)a.batch * a.seqlen_kv;
+  const uint64_t kv_rows = a.block_table != nullptr ? (uint64_t)a.num_pages * a.page_size
+                                                    : (uint64_t)a.batch * a.seqlen_kv;
   if (!make_map(&p.tm_kv, a.kv, kDim, kv_rows, dt) || !make_map(&p.tm_kpe, a.k_pe, kPeDim, kv_rows, dt) ||
       !make_map3(&p.tm_q, a.q, kDim, a.heads, a.batch, dt) ||
       !make_map3(&p.tm_qpe, a.q_pe, kPeDim, a.heads, a.batch, dt))
     return cudaErrorInvalidValue;
   p.out_f32 = a.out_dtype == MLA_DTYPE_F32 ? 1 : 0;
-  p.fuse_merge = variant == 0 ? 1 : 0;
+  (void)variant;   // the combine launch (variant 1, ragged calls) takes what the kernel does not merge
+  p.fuse_max = kFuseMaxPieces;
   if (!(p.out_f32 ? make_map3(&p.tm_out, a.out, kDim, a.heads, a.batch, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4)
                   : make_map3(&p.tm_out, a.out, kDim, a.heads, a.batch, dt)))
     return cudaErrorInvalidValue;
@@ -1379,6 +1510,11 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
   p.pairs = pairs;
   p.maxp = a.plan.extra;
   p.sl2 = a.softmax_scale * kLog2e;
+  p.cu_tiles = a.cu_tiles;
+  p.seqlens = a.seqlens;
+  p.block_table = a.block_table;
+  p.page_size = a.page_size;
+  p.max_pages = a.max_pages;
   if (a.dtype == MLA_DTYPE_BF16)
     mla_sm100_decode_kernel<__nv_bfloat16>
         <<<2 * pairs, kThreads, Smem<__nv_bfloat16>::kBytes, a.stream>>>(p);
@@ -1396,16 +1532,46 @@ cudaError_t launch_sm100_combine(const DecodeArgs& a) {
   const dim3 grid(kHeads, vb);
   if (a.out_dtype == MLA_DTYPE_F32)
     mla_pair_combine_kernel<float><<<grid, 128, 0, a.stream>>>(
-        a.part_lse, a.part_o, static_cast<float*>(a.out), a.lse, total, nt, a.plan.bpc, a.plan.extra, a.heads,
-        hg);
+        a.part_lse, a.part_o, static_cast<float*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb, a.heads,
+        hg, kFuseMaxPieces);
   else if (a.dtype == MLA_DTYPE_BF16)
     mla_pair_combine_kernel<__nv_bfloat16><<<grid, 128, 0, a.stream>>>(
-        a.part_lse, a.part_o, static_cast<__nv_bfloat16*>(a.out), a.lse, total, nt, a.plan.bpc,
-        a.plan.extra, a.heads, hg);
+        a.part_lse, a.part_o, static_cast<__nv_bfloat16*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb,
+        a.heads, hg, kFuseMaxPieces);
   else
     mla_pair_combine_kernel<__half><<<grid, 128, 0, a.stream>>>(
-        a.part_lse, a.part_o, static_cast<__half*>(a.out), a.lse, total, nt, a.plan.bpc, a.plan.extra,
-        a.heads, hg);
+        a.part_lse, a.part_o, static_cast<__half*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb, a.heads,
+        hg, kFuseMaxPieces);
+  return cudaGetLastError();
+}
+
+}  // namespace mla
+
+namespace mla {
+
+SplitPlan sm100_plan_ragged(int batch, int heads, int max_seqlen_kv, const MlaCfg& cfg) {
+  SplitPlan pl{};
+  pl.block_n = sm100::kTile;
+  const int nt = (max_seqlen_kv + sm100::kTile - 1) / sm100::kTile;
+  const long long total_max = (long long)batch * head_groups(heads) * nt;
+  int pairs = cfg.num_split > 0 ? cfg.num_split : 0;
+  int cap = sm100::current_max_pairs();
+  if (cap <= 0) cap = 74;
+  if (pairs == 0 || pairs > cap) pairs = cap;
+  if (pairs > sm100::kMaxPairs) pairs = sm100::kMaxPairs;
+  if ((long long)pairs > total_max) pairs = (int)(total_max > 0 ? total_max : 1);
+  pl.ns = pairs * 2;
+  pl.bpc = pairs;
+  pl.extra = 2;
+  pl.part_rows = (long long)pairs * 2 * sm100::kHeads;
+  pl.needs_combine = true;
+  return pl;
+}
+
+cudaError_t launch_sm100_ragged_plan(const DecodeArgs& a) {
+  const int elem = a.out_dtype == MLA_DTYPE_F32 ? 4 : 2;
+  sm100::mla_ragged_plan_kernel<<<1, 1024, 0, a.stream>>>(a.seqlens, a.batch, a.heads, head_groups(a.heads),
+                                                   a.seqlen_kv, a.cu_tiles, a.out, a.lse, elem);
   return cudaGetLastError();
 }
 

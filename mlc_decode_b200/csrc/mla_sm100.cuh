@@ -17,7 +17,13 @@ SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int
 // Enqueue the tensor-core split-KV kernel; partials go to a.part_o/a.part_lse.
 cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant);
 
-// Enqueue the combine of split sequences for plans whose variant is 1 (no in-kernel merge).
+// Plan of a ragged call (per-sequence lengths): max_seqlen_kv bounds every length.
+SplitPlan sm100_plan_ragged(int batch, int heads, int max_seqlen_kv, const MlaCfg& cfg);
+
+// Enqueue the ragged plan kernel (tile prefix sums into a.cu_tiles, empty outputs).
+cudaError_t launch_sm100_ragged_plan(const DecodeArgs& a);
+
+// Enqueue the combine of split sequences the decode kernel did not merge itself.
 cudaError_t launch_sm100_combine(const DecodeArgs& a);
 
 }  // namespace mla

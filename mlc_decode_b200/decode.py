@@ -204,3 +204,86 @@ def combine(part_lse: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor, lse
         stream = torch.cuda.current_stream(part_lse.device).cuda_stream
     capi.combine(part_lse.data_ptr(), part_o.data_ptr(), ns, b, h, out.data_ptr(), lse_ptr,
                  out_types[out.dtype], stream)
+
+
+class MlaPagedDecodeKernel:
+    """Decode over KV caches of different lengths, optionally paged.
+
+    ``kernel(q, q_pe, kv_cache, k_pe_cache, cache_seqlens, out, lse=None,
+    block_table=None)``: ``cache_seqlens`` int32 [batch] gives each sequence's
+    KV rows (at most ``max_seqlen_kv``).  Without ``block_table`` the caches are
+    [batch, max_seqlen_kv, 1, 512] / [..., 64]; with it (int32 [batch,
+    max_pages]) they are pages [num_pages, page_size, 1, 512] / [..., 64] and
+    row r of sequence b is row r % page_size of page block_table[b, r //
+    page_size].  page_size is a multiple of 64.  No counterpart in the
+    reference (one kv_ctx per call there); the C entry point is
+    mla_decode_paged.
+    """
+
+    def __init__(self, batch, heads, max_seqlen_kv, cfg=None, softmax_scale=None):
+        self.batch, self.heads, self.max_seqlen_kv = int(batch), int(heads), int(max_seqlen_kv)
+        self.cfg = dict(cfg or {})
+        if softmax_scale is not None:
+            self.cfg["softmax_scale"] = float(softmax_scale)
+        self._ccfg = capi.make_cfg(self.cfg)
+        capi.load()
+        self._ws = {}
+        self._lock = threading.Lock()
+
+    def workspace_bytes(self, dtype: torch.dtype) -> int:
+        return capi.paged_workspace_bytes(self.batch, self.heads, self.max_seqlen_kv, _DTYPES[dtype], self._ccfg)
+
+    def _workspace(self, device, dtype):
+        key = (device.index, dtype)
+        ws = self._ws.get(key)
+        if ws is None:
+            with self._lock:
+                ws = self._ws.get(key)
+                if ws is None:
+                    # zeroed once: status word and piece counters start at zero
+                    ws = torch.zeros(self.workspace_bytes(dtype), dtype=torch.uint8, device=device)
+                    self._ws[key] = ws
+        return ws
+
+    def device_status(self, device, dtype) -> int:
+        """Status word the kernel leaves in the workspace (0 = no timeout)."""
+        ws = self._ws.get((torch.device(device).index, dtype))
+        if ws is None or ws.numel() < 4:
+            return 0
+        return int(ws[:4].view(torch.int32).item())
+
+    def __call__(self, q, q_pe, kv_cache, k_pe_cache, cache_seqlens, out, lse=None, block_table=None):
+        b, h, smax = self.batch, self.heads, self.max_seqlen_kv
+        dtype = q.dtype if isinstance(q, torch.Tensor) else None
+        if dtype not in _DTYPES:
+            raise ValueError(f"q must be float16 or bfloat16, got {dtype}")
+        dev = q.device
+        _check_tensor("q", q, (b, h, DIM), dtype, None)
+        _check_tensor("q_pe", q_pe, (b, h, PE_DIM), dtype, dev)
+        _check_tensor("out", out, (b, h, DIM), dtype, dev)
+        _check_tensor("cache_seqlens", cache_seqlens, (b,), torch.int32, dev)
+        if block_table is None:
+            _check_tensor("kv_cache", kv_cache, (b, smax, 1, DIM), dtype, dev)
+            _check_tensor("k_pe_cache", k_pe_cache, (b, smax, 1, PE_DIM), dtype, dev)
+            bt_ptr, page_size, num_pages, max_pages = None, 0, 0, 0
+        else:
+            if kv_cache.dim() != 4:
+                raise ValueError("kv_cache must be [num_pages, page_size, 1, 512]")
+            num_pages, page_size = int(kv_cache.shape[0]), int(kv_cache.shape[1])
+            _check_tensor("kv_cache", kv_cache, (num_pages, page_size, 1, DIM), dtype, dev)
+            _check_tensor("k_pe_cache", k_pe_cache, (num_pages, page_size, 1, PE_DIM), dtype, dev)
+            if block_table.dim() != 2 or block_table.shape[0] != b:
+                raise ValueError(f"block_table must be [batch, max_pages], got {tuple(block_table.shape)}")
+            max_pages = int(block_table.shape[1])
+            _check_tensor("block_table", block_table, (b, max_pages), torch.int32, dev)
+            bt_ptr = block_table.data_ptr()
+        lse_ptr = None
+        if lse is not None:
+            _check_tensor("lse", lse, (b, h), torch.float32, dev)
+            lse_ptr = lse.data_ptr()
+        ws = self._workspace(dev, dtype)
+        with torch.cuda.device(dev):
+            stream = torch.cuda.current_stream(dev).cuda_stream
+        capi.decode_paged(q.data_ptr(), q_pe.data_ptr(), kv_cache.data_ptr(), k_pe_cache.data_ptr(), bt_ptr,
+                          cache_seqlens.data_ptr(), out.data_ptr(), lse_ptr, ws.data_ptr(), ws.numel(), b, h, smax,
+                          page_size, num_pages, max_pages, _DTYPES[dtype], self._ccfg, stream)
