@@ -63,11 +63,18 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="budget of host-core time for the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--paged", type=int, default=0, metavar="PAGE_SIZE",
+                    help="decode through mla_decode_paged with KV in shuffled pages of this many rows")
+    ap.add_argument("--ragged", action="store_true",
+                    help="with --paged: per-sequence lengths drawn uniformly from [1, kv_ctx] (seeded)")
     return ap.parse_args()
 
 
 def workload_name(a):
-    return f"mla_decode b{a.batch}/gpu h{a.heads} s{a.kv_ctx} {a.dtype} (dim 512+64, kv_heads 1)"
+    name = f"mla_decode b{a.batch}/gpu h{a.heads} s{a.kv_ctx} {a.dtype} (dim 512+64, kv_heads 1)"
+    if a.paged:
+        name += f", paged KV ({a.paged}-row pages" + (", ragged lengths)" if a.ragged else ")")
+    return name
 
 
 def load_peaks():
@@ -214,7 +221,7 @@ def run_ours(a, rank, world, local_rank):
     import torch
     import torch.distributed as dist
 
-    from mlc_decode_b200 import MlaDecodeKernel
+    from mlc_decode_b200 import MlaDecodeKernel, MlaPagedDecodeKernel
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -223,15 +230,49 @@ def run_ours(a, rank, world, local_rank):
     cfg = {"kernel": a.kernel}
     if a.num_split:
         cfg["num_split"] = a.num_split
-    kern = MlaDecodeKernel(b, h, 1, s, cfg=cfg)
 
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     q = torch.randn(b, h, 512, device=dev, generator=g).to(tdt)
     q_pe = torch.randn(b, h, 64, device=dev, generator=g).to(tdt)
-    kv = torch.randn(b, s, 1, 512, device=dev, generator=g).to(tdt)
-    k_pe = torch.randn(b, s, 1, 64, device=dev, generator=g).to(tdt)
+    lens = [s] * b
+    if a.paged:
+        # KV rows scattered over shuffled pages (the serving layout), block table per sequence
+        if a.ragged:
+            gl = torch.Generator().manual_seed(99 + rank)
+            lens = [int(x) for x in torch.randint(1, s + 1, (b,), generator=gl)]
+        ps = a.paged
+        npg = [-(-L // ps) for L in lens]
+        num_pages = sum(npg)
+        perm = torch.randperm(num_pages, generator=torch.Generator().manual_seed(7 + rank))
+        table = torch.zeros(b, max(npg), dtype=torch.int32)
+        k = 0
+        for bb in range(b):
+            for i in range(npg[bb]):
+                table[bb, i] = int(perm[k])
+                k += 1
+        kv = torch.randn(num_pages, ps, 1, 512, device=dev, generator=g).to(tdt)
+        k_pe = torch.randn(num_pages, ps, 1, 64, device=dev, generator=g).to(tdt)
+        table = table.to(dev)
+        seqlens = torch.tensor(lens, dtype=torch.int32, device=dev)
+        pkern = MlaPagedDecodeKernel(b, h, s, cfg=cfg)
+
+        class _Paged:
+            def __call__(self, q_, qp_, kv_, kp_, out_):
+                pkern(q_, qp_, kv_, kp_, seqlens, out_, block_table=table)
+
+            splitkv = __call__
+
+            def combine_ws(self, out_):
+                pass
+
+        kern = _Paged()
+        launches = 3
+    else:
+        kern = MlaDecodeKernel(b, h, 1, s, cfg=cfg)
+        kv = torch.randn(b, s, 1, 512, device=dev, generator=g).to(tdt)
+        k_pe = torch.randn(b, s, 1, 64, device=dev, generator=g).to(tdt)
+        launches = kern.launches_per_call(tdt)
     out = torch.empty_like(q)
-    launches = kern.launches_per_call(tdt)
 
     def barrier():
         if world > 1:
@@ -305,7 +346,7 @@ def run_ours(a, rank, world, local_rank):
     if rank != 0:
         return
     peaks = load_peaks()
-    bytes_alg, flops_alg = algorithmic(b, h, s)
+    bytes_alg, flops_alg = algorithmic(1, h, sum(lens))
     achieved = bytes_alg / (dec_us * 1e-6) / 1e9
     t_roof_us = max(bytes_alg / (peaks["hbm_gbs"] * 1e9), flops_alg / (peaks["bf16_tflops"] * 1e12)) * 1e6
     line = {
@@ -320,7 +361,8 @@ def run_ours(a, rank, world, local_rank):
                          % (bytes_alg / 1e6)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     "traffic": traffic_from_profiles(a), "kernel": "split-KV decode kernel",
+                     "traffic": None if a.paged else traffic_from_profiles(a),
+                     "kernel": "paged decode call (plan + decode + combine)" if a.paged else "split-KV decode kernel",
                      "kernel_us": round(dec_us, 3), "peak_source": peaks["source"]},
         "mla_roofline": {"t_roof_us": round(t_roof_us, 3),
                          "frac": round(t_roof_us / us_call, 4),
@@ -332,7 +374,9 @@ def run_ours(a, rank, world, local_rank):
         "gpu_launches": K * launches,
         "clocks": clk,
     }
-    if world == 1 and not a.no_cpu_baseline:
+    if a.paged:
+        line["config"]["kv_rows_total"] = sum(lens)
+    if world == 1 and not a.no_cpu_baseline and not a.paged:
         times, bs, cores = cpu_time_per_call(a, a.cpu_seconds)
         cpu_us = statistics.median(times) * 1e6 * (b / bs)
         line["cpu_baseline"] = {"value": round(cpu_us, 3), "unit": UNIT, "cores": cores, "kind": "port",

@@ -190,9 +190,10 @@ int32_t mla_decode_partial(const void* q, const void* q_pe, const void* kv,
  *                 kv_cache [num_pages, page_size, 1, 512] and
  *                 k_pe_cache [num_pages, page_size, 1, 64]; row r of sequence b
  *                 is row r % page_size of page block_table[b][r / page_size].
- *                 page_size is a multiple of 64 and
- *                 max_pages_per_seq x page_size >= max_seqlen_kv; entries past a
- *                 sequence's length are not read.
+ *                 page_size is a multiple of 64; lengths are also clamped to
+ *                 max_pages_per_seq x page_size; entries past a sequence's
+ *                 length are not read, and rows of its last page past the length
+ *                 must hold finite values (they are masked).
  * q, q_pe, out, lse, dtype and cfg as in mla_decode_fwd (tensor-core kernel only;
  * cfg->num_split = CTA pairs).  `workspace` holds mla_paged_workspace_bytes()
  * bytes, 256-byte aligned, zero before the first call (every call leaves its

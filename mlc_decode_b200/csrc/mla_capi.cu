@@ -439,11 +439,10 @@ int32_t mla_decode_paged(const void* q, const void* q_pe, const void* kv_cache, 
   }
   if (block_table != nullptr) {
     if (page_size < 64 || page_size % 64 != 0 || num_pages < 1 || max_pages_per_seq < 1 ||
-        (long long)max_pages_per_seq * page_size < max_seqlen_kv ||
         (long long)num_pages * page_size >= (1ll << 31) - 256) {
-      set_error("%s: page_size must be a multiple of 64 and max_pages_per_seq x page_size >= max_seqlen_kv "
-                "(page_size %d, num_pages %d, max_pages_per_seq %d, max_seqlen_kv %d)",
-                fn, page_size, num_pages, max_pages_per_seq, max_seqlen_kv);
+      set_error("%s: page_size must be a positive multiple of 64, with num_pages x page_size rows "
+                "below 2^31 (page_size %d, num_pages %d, max_pages_per_seq %d)",
+                fn, page_size, num_pages, max_pages_per_seq);
       return MLA_ERR_ARG;
     }
   }
@@ -482,7 +481,7 @@ int32_t mla_decode_paged(const void* q, const void* q_pe, const void* kv_cache, 
   a.page_size = block_table != nullptr ? page_size : 0;
   a.num_pages = block_table != nullptr ? num_pages : 0;
   a.max_pages = block_table != nullptr ? max_pages_per_seq : 0;
-  cudaError_t err = launch_sm100_ragged_plan(a);
+  cudaError_t err = launch_sm100_ragged_plan(a);   // lengths clamped as the decode kernel does
   if (err == cudaSuccess) err = launch_sm100_decode(a, 1);
   if (err == cudaSuccess) err = launch_sm100_combine(a);
   if (err != cudaSuccess) {

@@ -292,10 +292,18 @@ struct PieceIter {
 
 // KV rows of virtual sequence v, and the row in the KV tensor map of row `row`
 // of sequence `seq` (contiguous [b, seqlen] rows, or a page of block_table).
+// Longest sequence a call can hold: max_seqlen_kv, and for a paged call the rows
+// its block table covers.
+__device__ __forceinline__ int max_len(const Params& p) {
+  if (p.block_table == nullptr) return p.seqlen;
+  const long long cover = (long long)p.max_pages * p.page_size;
+  return cover < p.seqlen ? (int)cover : p.seqlen;
+}
 __device__ __forceinline__ int seq_len(const Params& p, int v) {
   if (p.seqlens == nullptr) return p.seqlen;
-  const int len = __ldg(p.seqlens + vseq_seq(p, v));   // clamped to [0, seqlen]: see the plan kernel
-  return len < 0 ? 0 : (len > p.seqlen ? p.seqlen : len);
+  const int len = __ldg(p.seqlens + vseq_seq(p, v));   // clamped to [0, max_len]: see the plan kernel
+  const int cap = max_len(p);
+  return len < 0 ? 0 : (len > cap ? cap : len);
 }
 __device__ __forceinline__ int kv_row(const Params& p, int seq, int row, int len) {
   if (p.block_table == nullptr) return seq * p.seqlen + row;
@@ -341,9 +349,10 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
   Piece pc;
   // K units stream straight across piece boundaries: Q has its own loader thread
   while (it.next(&pc)) {
+    const int kseq = vseq_seq(p, pc.bb), klen = seq_len(p, pc.bb);
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j) {
-      const int y = kv_row(p, vseq_seq(p, pc.bb), j * kTile + 64 * (int)rank, seq_len(p, pc.bb));
+      const int y = kv_row(p, kseq, j * kTile + 64 * (int)rank, klen);
 #pragma unroll 1
       for (int u = 0; u < 5; ++u) {
         if (!wait_bar(c, kempty0 + 8 * ring.stage, ring.phase ^ 1u, kErrKLoad)) return;
@@ -445,8 +454,10 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
   Piece pc;
   while (it.next(&pc)) {
 #pragma unroll 1
+    const int vseq = vseq_seq(p, pc.bb), vlen = seq_len(p, pc.bb);
     for (int j = pc.first; j < pc.end; ++j) {
-      const int vseq = vseq_seq(p, pc.bb), vlen = seq_len(p, pc.bb);
+      // both token halves' rows, looked up before the ring waits (page-table loads)
+      const int yv0 = kv_row(p, vseq, j * kTile, vlen), yv1 = kv_row(p, vseq, j * kTile + 64, vlen);
 #pragma unroll 1
       for (int u = 0; u < 4; ++u) {
         const int nh = u >> 1, th = u & 1;
@@ -456,7 +467,7 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
         const uint32_t bar = vfull0_leader + 8 * ring.stage;
         const int x = 256 * nh + 128 * (int)rank;
         // the latent rows' last read
-        const int yv = kv_row(p, vseq, j * kTile + 64 * th, vlen);
+        const int yv = th == 0 ? yv0 : yv1;
         ptx::tma_load_2d_pair_hint(dst, &p.tm_kv, bar, x, yv, once);
         ptx::tma_load_2d_pair_hint(dst + kChunkBytes, &p.tm_kv, bar, x + 64, yv, once);
         ring.advance();
@@ -1295,7 +1306,7 @@ mla_ragged_plan_kernel(const int* __restrict__ seqlens, int batch, int heads, in
   }
   if (tid == 1023) cu[vb] = s_part[1023];
   for (int row = tid; row < batch * heads; row += 1024) {
-    if (seqlens[row / heads] > 0) continue;
+    if (seqlens[row / heads] > 0 && max_len > 0) continue;
     uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(out) + (size_t)row * kDim * out_elem_bytes);
     for (int i = 0; i < kDim * out_elem_bytes / 16; ++i) o[i] = make_uint4(0u, 0u, 0u, 0u);
     if (lse != nullptr) lse[row] = -INFINITY;
@@ -1570,8 +1581,10 @@ SplitPlan sm100_plan_ragged(int batch, int heads, int max_seqlen_kv, const MlaCf
 
 cudaError_t launch_sm100_ragged_plan(const DecodeArgs& a) {
   const int elem = a.out_dtype == MLA_DTYPE_F32 ? 4 : 2;
+  int cap = a.seqlen_kv;
+  if (a.block_table != nullptr && (long long)a.max_pages * a.page_size < cap) cap = a.max_pages * a.page_size;
   sm100::mla_ragged_plan_kernel<<<1, 1024, 0, a.stream>>>(a.seqlens, a.batch, a.heads, head_groups(a.heads),
-                                                   a.seqlen_kv, a.cu_tiles, a.out, a.lse, elem);
+                                                          cap, a.cu_tiles, a.out, a.lse, elem);
   return cudaGetLastError();
 }
 
