@@ -212,6 +212,35 @@ int32_t mla_decode_paged(const void* q, const void* q_pe, const void* kv_cache,
                          const MlaCfg* cfg, void* stream);
 
 /*
+ * mla_decode_paged for multi-token decode steps and grouped KV heads.  No
+ * counterpart in the reference (baseline_mla.py:16 asserts kv_heads == 1 and
+ * its query has one position per sequence); its ref_program's head grouping
+ * (baseline_mla.py:179-186: query head j reads KV head j / (heads / kv_heads))
+ * is kept.
+ *
+ *   q, out     [batch, q_len, heads, 512]   q_pe [batch, q_len, heads, 64]
+ *   lse        [batch, q_len, heads] float32, optional (natural log)
+ *   kv_cache   [batch, max_seqlen_kv, kv_heads, 512] (no block_table) or
+ *              [num_pages, page_size, kv_heads, 512]; k_pe_cache likewise with 64
+ *   cache_seqlens  int32 [batch] KV rows per sequence, or NULL (all
+ *              max_seqlen_kv, capped by the page table's cover when paged)
+ *
+ * Query position t of a sequence with L rows attends to its first
+ * L - (q_len - 1 - t) rows (the step's q_len new tokens are the last rows of the
+ * cache; causal within the step); a position with no rows gets out = 0,
+ * lse = -inf.  heads must be a multiple of kv_heads.  Workspace from
+ * mla_decode_ext_workspace_bytes, same rules as mla_decode_paged (q_len = 1,
+ * kv_heads = 1 is exactly mla_decode_paged).
+ */
+size_t mla_decode_ext_workspace_bytes(int32_t batch, int32_t q_len, int32_t heads, int32_t kv_heads,
+                                      int32_t max_seqlen_kv, int32_t dtype, const MlaCfg* cfg);
+int32_t mla_decode_ext(const void* q, const void* q_pe, const void* kv_cache, const void* k_pe_cache,
+                       const int32_t* block_table, const int32_t* cache_seqlens, void* out, float* lse,
+                       void* workspace, size_t workspace_bytes, int32_t batch, int32_t q_len, int32_t heads,
+                       int32_t kv_heads, int32_t max_seqlen_kv, int32_t page_size, int32_t num_pages,
+                       int32_t max_pages_per_seq, int32_t dtype, const MlaCfg* cfg, void* stream);
+
+/*
  * mla_decode_fwd without a workspace argument, for callers that cannot
  * allocate device memory where they decode (code running under CUDA-graph
  * capture, servers that reserve all memory up front and forbid allocation on

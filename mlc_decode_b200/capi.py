@@ -26,7 +26,7 @@ EXPORTED_SYMBOLS = ("mla_abi_version", "mla_last_error", "mla_split_plan",
                     "mla_workspace_bytes", "mla_decode_fwd", "mla_decode_splitkv",
                     "mla_decode_combine_ws", "mla_combine", "mla_decode_fwd_noalloc",
                     "mla_describe_plan", "mla_decode_partial", "mla_paged_workspace_bytes",
-                    "mla_decode_paged")
+                    "mla_decode_paged", "mla_decode_ext_workspace_bytes", "mla_decode_ext")
 
 
 class MlaCfg(ctypes.Structure):
@@ -91,6 +91,11 @@ def load(build_if_missing: bool = True):
         lib.mla_decode_paged.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, sz, i32, i32, i32, i32, i32, i32,
                                          i32, ctypes.POINTER(MlaCfg), vp]
         lib.mla_decode_paged.restype = i32
+        lib.mla_decode_ext_workspace_bytes.argtypes = [i32, i32, i32, i32, i32, i32, ctypes.POINTER(MlaCfg)]
+        lib.mla_decode_ext_workspace_bytes.restype = sz
+        lib.mla_decode_ext.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, sz, i32, i32, i32, i32, i32, i32, i32,
+                                       i32, i32, ctypes.POINTER(MlaCfg), vp]
+        lib.mla_decode_ext.restype = i32
         lib.mla_decode_combine_ws.argtypes = [vp, vp, vp, sz, i32, i32, i32, i32,
                                               ctypes.POINTER(MlaCfg), vp]
         lib.mla_decode_combine_ws.restype = i32
@@ -196,6 +201,27 @@ def decode_paged(q, q_pe, kv_cache, k_pe_cache, block_table, cache_seqlens, out,
     check(load().mla_decode_paged(q, q_pe, kv_cache, k_pe_cache, block_table, cache_seqlens, out, lse, ws,
                                   ws_bytes, int(batch), int(heads), int(max_seqlen_kv), int(page_size),
                                   int(num_pages), int(max_pages), int(dtype), ctypes.byref(cfg), stream))
+
+
+def ext_workspace_bytes(batch, q_len, heads, kv_heads, max_seqlen_kv, dtype, cfg: MlaCfg) -> int:
+    lib = load()
+    n = lib.mla_decode_ext_workspace_bytes(int(batch), int(q_len), int(heads), int(kv_heads), int(max_seqlen_kv),
+                                           int(dtype), ctypes.byref(cfg))
+    if n == 0:
+        msg = last_error()
+        if msg:
+            raise MlaError(1, msg)
+    return int(n)
+
+
+def decode_ext(q, q_pe, kv_cache, k_pe_cache, block_table, cache_seqlens, out, lse, ws, ws_bytes, batch, q_len,
+               heads, kv_heads, max_seqlen_kv, page_size, num_pages, max_pages, dtype, cfg: MlaCfg, stream) -> None:
+    """mla_decode_ext: q_len query positions per sequence (causal within the step), kv_heads KV heads,
+    per-sequence KV lengths (cache_seqlens may be None) and an optional page table."""
+    check(load().mla_decode_ext(q, q_pe, kv_cache, k_pe_cache, block_table, cache_seqlens, out, lse, ws, ws_bytes,
+                                int(batch), int(q_len), int(heads), int(kv_heads), int(max_seqlen_kv),
+                                int(page_size), int(num_pages), int(max_pages), int(dtype), ctypes.byref(cfg),
+                                stream))
 
 
 def decode_splitkv(q, q_pe, kv, k_pe, out, lse, ws, ws_bytes, batch, heads, seqlen_kv, dtype,

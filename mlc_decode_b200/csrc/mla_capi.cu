@@ -382,25 +382,33 @@ struct PagedLayout {
   size_t counters_off, cu_off, lse_off, o_off, total;
 };
 
-int paged_layout(int batch, int heads, int max_seqlen_kv, int dtype, const MlaCfg* cfg, PagedLayout* L) {
+// Query side: batch x q_len x kv_heads query sequences of heads / kv_heads rows.
+int paged_layout(const char* fn, int batch, int q_len, int heads, int kv_heads, int max_seqlen_kv, int dtype,
+                 const MlaCfg* cfg, PagedLayout* L) {
   int rc = check_shape(batch, heads, max_seqlen_kv, dtype);
   if (rc != MLA_OK) return rc;
+  if (q_len < 1 || kv_heads < 1 || heads % kv_heads != 0) {
+    set_error("%s: q_len and kv_heads must be >= 1 with heads a multiple of kv_heads (q_len %d, heads %d, "
+              "kv_heads %d)", fn, q_len, heads, kv_heads);
+    return MLA_ERR_ARG;
+  }
   MlaCfg c{};
   if (cfg != nullptr) c = *cfg;
   if (c.kernel == MLA_KERNEL_SIMT) {
-    set_error("mla_decode_paged: runs on the tensor-core kernel only (kernel = auto or tc)");
+    set_error("%s: runs on the tensor-core kernel only (kernel = auto or tc)", fn);
     return MLA_ERR_UNSUPPORTED;
   }
-  if (!sm100_supports(batch, heads, max_seqlen_kv)) {
-    set_error("mla_decode_paged: shape outside the tensor-core kernel (batch %d, heads %d, max_seqlen_kv %d)",
-              batch, heads, max_seqlen_kv);
+  if (!sm100_supports_ext(batch, q_len, heads, kv_heads, max_seqlen_kv)) {
+    set_error("%s: shape outside the tensor-core kernel (batch %d, q_len %d, heads %d, kv_heads %d, "
+              "max_seqlen_kv %d)", fn, batch, q_len, heads, kv_heads, max_seqlen_kv);
     return MLA_ERR_UNSUPPORTED;
   }
-  L->plan = sm100_plan_ragged(batch, heads, max_seqlen_kv, c);
-  const size_t vb = (size_t)batch * head_groups(heads);
+  const int qb = batch * q_len * kv_heads, g = heads / kv_heads;
+  L->plan = sm100_plan_ragged(qb, g, max_seqlen_kv, c);
+  const size_t vb = (size_t)qb * head_groups(g);
   const size_t rows = (size_t)L->plan.part_rows;
   L->counters_off = kStatusBytes;
-  L->cu_off = L->counters_off + counter_bytes(batch, heads);
+  L->cu_off = L->counters_off + counter_bytes(qb, g);
   L->lse_off = L->cu_off + align_up((vb + 1) * sizeof(uint32_t), 256);
   L->o_off = L->lse_off + align_up(rows * sizeof(float), 256);
   L->total = L->o_off + rows * kDim * sizeof(float);
@@ -414,22 +422,32 @@ extern "C" {
 
 size_t mla_paged_workspace_bytes(int32_t batch, int32_t heads, int32_t max_seqlen_kv, int32_t dtype,
                                  const MlaCfg* cfg) {
+  return mla_decode_ext_workspace_bytes(batch, 1, heads, 1, max_seqlen_kv, dtype, cfg);
+}
+
+size_t mla_decode_ext_workspace_bytes(int32_t batch, int32_t q_len, int32_t heads, int32_t kv_heads,
+                                      int32_t max_seqlen_kv, int32_t dtype, const MlaCfg* cfg) {
   g_last_error.clear();
   PagedLayout L;
-  if (paged_layout(batch, heads, max_seqlen_kv, dtype, cfg, &L) != MLA_OK) return 0;
+  if (paged_layout("mla_decode_ext", batch, q_len, heads, kv_heads, max_seqlen_kv, dtype, cfg, &L) != MLA_OK)
+    return 0;
   return L.total;
 }
 
-int32_t mla_decode_paged(const void* q, const void* q_pe, const void* kv_cache, const void* k_pe_cache,
-                         const int32_t* block_table, const int32_t* cache_seqlens, void* out, float* lse,
-                         void* workspace, size_t workspace_bytes, int32_t batch, int32_t heads,
-                         int32_t max_seqlen_kv, int32_t page_size, int32_t num_pages,
-                         int32_t max_pages_per_seq, int32_t dtype, const MlaCfg* cfg, void* stream) {
-  const char* fn = "mla_decode_paged";
+}  // extern "C"
+
+namespace mla {
+namespace {
+
+int decode_ext(const char* fn, const void* q, const void* q_pe, const void* kv_cache, const void* k_pe_cache,
+               const int32_t* block_table, const int32_t* cache_seqlens, void* out, float* lse, void* workspace,
+               size_t workspace_bytes, int32_t batch, int32_t q_len, int32_t heads, int32_t kv_heads,
+               int32_t max_seqlen_kv, int32_t page_size, int32_t num_pages, int32_t max_pages_per_seq,
+               int32_t dtype, const MlaCfg* cfg, void* stream) {
   PagedLayout L;
-  int rc = paged_layout(batch, heads, max_seqlen_kv, dtype, cfg, &L);
+  int rc = paged_layout(fn, batch, q_len, heads, kv_heads, max_seqlen_kv, dtype, cfg, &L);
   if (rc != MLA_OK) return rc;
-  if (!q || !q_pe || !kv_cache || !k_pe_cache || !cache_seqlens || !out) {
+  if (!q || !q_pe || !kv_cache || !k_pe_cache || !out) {
     set_error("%s: null pointer", fn);
     return MLA_ERR_ARG;
   }
@@ -461,6 +479,8 @@ int32_t mla_decode_paged(const void* q, const void* q_pe, const void* kv_cache, 
   a.lse = lse;
   a.batch = batch;
   a.heads = heads;
+  a.q_len = q_len;
+  a.kv_heads = kv_heads;
   a.seqlen_kv = max_seqlen_kv;
   a.dtype = dtype;
   a.softmax_scale = (cfg != nullptr && cfg->softmax_scale != 0.f) ? cfg->softmax_scale : 1.0f / sqrtf((float)kQkDim);
@@ -489,6 +509,35 @@ int32_t mla_decode_paged(const void* q, const void* q_pe, const void* kv_cache, 
     return MLA_ERR_CUDA;
   }
   return MLA_OK;
+}
+
+}  // namespace
+}  // namespace mla
+
+extern "C" {
+
+int32_t mla_decode_paged(const void* q, const void* q_pe, const void* kv_cache, const void* k_pe_cache,
+                         const int32_t* block_table, const int32_t* cache_seqlens, void* out, float* lse,
+                         void* workspace, size_t workspace_bytes, int32_t batch, int32_t heads,
+                         int32_t max_seqlen_kv, int32_t page_size, int32_t num_pages,
+                         int32_t max_pages_per_seq, int32_t dtype, const MlaCfg* cfg, void* stream) {
+  if (cache_seqlens == nullptr) {
+    set_error("mla_decode_paged: null pointer");
+    return MLA_ERR_ARG;
+  }
+  return decode_ext("mla_decode_paged", q, q_pe, kv_cache, k_pe_cache, block_table, cache_seqlens, out, lse,
+                    workspace, workspace_bytes, batch, 1, heads, 1, max_seqlen_kv, page_size, num_pages,
+                    max_pages_per_seq, dtype, cfg, stream);
+}
+
+int32_t mla_decode_ext(const void* q, const void* q_pe, const void* kv_cache, const void* k_pe_cache,
+                       const int32_t* block_table, const int32_t* cache_seqlens, void* out, float* lse,
+                       void* workspace, size_t workspace_bytes, int32_t batch, int32_t q_len, int32_t heads,
+                       int32_t kv_heads, int32_t max_seqlen_kv, int32_t page_size, int32_t num_pages,
+                       int32_t max_pages_per_seq, int32_t dtype, const MlaCfg* cfg, void* stream) {
+  return decode_ext("mla_decode_ext", q, q_pe, kv_cache, k_pe_cache, block_table, cache_seqlens, out, lse,
+                    workspace, workspace_bytes, batch, q_len, heads, kv_heads, max_seqlen_kv, page_size, num_pages,
+                    max_pages_per_seq, dtype, cfg, stream);
 }
 
 }  // extern "C"

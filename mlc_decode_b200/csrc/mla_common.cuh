@@ -122,9 +122,20 @@ struct DecodeArgs {
   int page_size, num_pages, max_pages;
   uint32_t* cu_tiles;      // workspace: flattened-tile prefix sums (batch x head groups + 1)
   int batch, heads, seqlen_kv, dtype;
+  // query positions per sequence (causal within the step) and KV heads (query
+  // heads [i*h/kv_heads, (i+1)*h/kv_heads) read KV head i); 0 means 1.
+  // Tensor-core kernel only.
+  int q_len, kv_heads;
   float softmax_scale;  // multiplies raw scores
   SplitPlan plan;
   cudaStream_t stream;
+};
+
+// Query side of a call as the tensor-core kernel sees it: qb = batch x q_len x
+// kv_heads query sequences of g = heads / kv_heads rows, hg groups of up to 128
+// rows each, vb = qb x hg virtual sequences.
+struct QShape {
+  int q_len, kv_heads, qb, g, hg, vb;
 };
 
 // CUDA-core split-KV kernel (mla_simt.cu).  Returns a cudaError_t.

@@ -133,14 +133,12 @@ struct Smem {
 };
 
 struct Params {
-  CUtensorMap tm_kv;    // [b*s, 512], box 64 x 64
-  CUtensorMap tm_kpe;   // [b*s, 64]
-  CUtensorMap tm_q;     // [b][h][512], box 64 x 64 x 1 (rows past h read as zero)
-  CUtensorMap tm_qpe;   // [b][h][64]
-  CUtensorMap tm_out;   // [b][h][512] output rows, box 64 x 64 x 1 (stores; rows past h not written)
+  CUtensorMap tm_kv;    // [b*s][kv_heads][512], box 64 x 1 x 64 rows
+  CUtensorMap tm_kpe;   // [b*s][kv_heads][64]
+  CUtensorMap tm_q;     // [qb][h][512], box 64 x 64 x 1 (rows past h read as zero)
+  CUtensorMap tm_qpe;   // [qb][h][64]
+  CUtensorMap tm_out;   // [qb][h][512] output rows, box 64 x 64 x 1 (stores; rows past h not written)
   CUtensorMap tm_part;  // [slots*128, 512] float32 partial rows, box 32 x 64 (stores)
-  const uint8_t* kv;    // raw rows, for L2 prefetch
-  const uint8_t* kpe;
   const uint8_t* q;     // raw Q rows, for L2 prefetch
   const uint8_t* qpe;
   void* out;
@@ -149,11 +147,17 @@ struct Params {
   float* part_lse;
   uint32_t* status;
   uint32_t* counters;   // [batch][2] pieces finished per (sequence, CTA rank); zero between calls
-  // Work units are "virtual sequences": sequence s, head group g (heads
-  // [128 g, 128 g + 128)) is v = s * hgroups + g; batch counts them.
+  // Work units are "virtual sequences".  The query side is qb = b x q_len x
+  // kv_heads query sequences qs = (s * q_len + t) * kv_heads + kvh (query
+  // position t of sequence s, the query heads of KV head kvh: rows of q/out
+  // that are contiguous in memory), each of `heads` rows; head group g (rows
+  // [128 g, 128 g + 128)) of query sequence qs is v = qs * hgroups + g, and
+  // batch counts them.  The KV side of v is sequence s, KV head kvh, and its
+  // first len(s) - (q_len - 1 - t) rows (causal within the decode step).
   uint32_t total_tiles;  // batch x tiles per sequence; total_tiles * (pairs + 1) < 2^32
   int batch, seqlen, nt, pairs, maxp;
-  int heads, hgroups;   // real head count; head groups of 128 per sequence
+  int heads, hgroups;   // query rows per query sequence (h / kv_heads); groups of 128 of them
+  int q_len, kv_heads;  // query positions per sequence, KV heads
   int out_f32;          // `out` is float32 (tm_out then has 32 x 64 float boxes)
   int fuse_max;         // sequences split into at most this many pieces are merged here
   // Ragged calls (per-sequence lengths, optionally paged KV): cu_tiles[v] is the
@@ -203,10 +207,29 @@ __device__ __forceinline__ bool aborted(const Ctx& c) {
   return *reinterpret_cast<volatile uint32_t*>(c.abort_local) != 0u;
 }
 
-// Sequence and first head row (within the sequence) of virtual sequence v.
+// Query sequence and first head row (within it) of virtual sequence v.
 __device__ __forceinline__ int vseq_seq(const Params& p, int v) { return p.hgroups == 1 ? v : v / p.hgroups; }
 __device__ __forceinline__ int vseq_head0(const Params& p, int v) {
   return p.hgroups == 1 ? 0 : (v % p.hgroups) * kHeads;
+}
+// KV sequence and KV head of virtual sequence v.
+__device__ __forceinline__ int vseq_kvseq(const Params& p, int v) {
+  const int qs = vseq_seq(p, v), per = p.q_len * p.kv_heads;
+  return per == 1 ? qs : qs / per;
+}
+__device__ __forceinline__ int vseq_kvh(const Params& p, int v) {
+  return p.kv_heads == 1 ? 0 : vseq_seq(p, v) % p.kv_heads;
+}
+// KV rows of query sequence qs: its sequence's length (nullptr: all max_len),
+// clamped to [0, max_len], less the rows the causal mask hides from position t.
+__device__ __forceinline__ int qseq_len(const int* seqlens, int qs, int q_len, int kv_heads, int max_len) {
+  int len = max_len;
+  if (seqlens != nullptr) {
+    len = __ldg(seqlens + qs / (q_len * kv_heads));
+    len = len < 0 ? 0 : (len > max_len ? max_len : len);
+  }
+  len -= q_len - 1 - (qs / kv_heads) % q_len;
+  return len < 0 ? 0 : len;
 }
 
 // One contiguous run of tiles of one (virtual) sequence inside a pair's range.
@@ -300,10 +323,9 @@ __device__ __forceinline__ int max_len(const Params& p) {
   return cover < p.seqlen ? (int)cover : p.seqlen;
 }
 __device__ __forceinline__ int seq_len(const Params& p, int v) {
-  if (p.seqlens == nullptr) return p.seqlen;
-  const int len = __ldg(p.seqlens + vseq_seq(p, v));   // clamped to [0, max_len]: see the plan kernel
-  const int cap = max_len(p);
-  return len < 0 ? 0 : (len > cap ? cap : len);
+  if (p.seqlens == nullptr && p.q_len == 1) return p.seqlen;
+  // the plan kernel counts tiles with the same lengths
+  return qseq_len(p.seqlens, vseq_seq(p, v), p.q_len, p.kv_heads, max_len(p));
 }
 __device__ __forceinline__ int kv_row(const Params& p, int seq, int row, int len) {
   if (p.block_table == nullptr) return seq * p.seqlen + row;
@@ -349,7 +371,7 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
   Piece pc;
   // K units stream straight across piece boundaries: Q has its own loader thread
   while (it.next(&pc)) {
-    const int kseq = vseq_seq(p, pc.bb), klen = seq_len(p, pc.bb);
+    const int kseq = vseq_kvseq(p, pc.bb), kvh = vseq_kvh(p, pc.bb), klen = seq_len(p, pc.bb);
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j) {
       const int y = kv_row(p, kseq, j * kTile + 64 * (int)rank, klen);
@@ -361,10 +383,10 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
         const uint32_t dst = sbase + S::kKRing + ring.stage * kStageBytes;
         const uint32_t bar = kfull0_leader + 8 * ring.stage;
         if (u < 4) {
-          ptx::tma_load_2d_pair_hint(dst, &p.tm_kv, bar, 128 * u, y, keep);
-          ptx::tma_load_2d_pair_hint(dst + kChunkBytes, &p.tm_kv, bar, 128 * u + 64, y, keep);
+          ptx::tma_load_3d_pair_hint(dst, &p.tm_kv, bar, 128 * u, kvh, y, keep);
+          ptx::tma_load_3d_pair_hint(dst + kChunkBytes, &p.tm_kv, bar, 128 * u + 64, kvh, y, keep);
         } else {
-          ptx::tma_load_2d_pair_hint(dst, &p.tm_kpe, bar, 0, y, once);
+          ptx::tma_load_3d_pair_hint(dst, &p.tm_kpe, bar, 0, kvh, y, once);
         }
         ring.advance();
       }
@@ -453,8 +475,8 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
   if (!wait_bar(c, ptx::smem_u32(&bars->q_go), 0u, kErrVLoad)) return;
   Piece pc;
   while (it.next(&pc)) {
+    const int vseq = vseq_kvseq(p, pc.bb), kvh = vseq_kvh(p, pc.bb), vlen = seq_len(p, pc.bb);
 #pragma unroll 1
-    const int vseq = vseq_seq(p, pc.bb), vlen = seq_len(p, pc.bb);
     for (int j = pc.first; j < pc.end; ++j) {
       // both token halves' rows, looked up before the ring waits (page-table loads)
       const int yv0 = kv_row(p, vseq, j * kTile, vlen), yv1 = kv_row(p, vseq, j * kTile + 64, vlen);
@@ -468,8 +490,8 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
         const int x = 256 * nh + 128 * (int)rank;
         // the latent rows' last read
         const int yv = th == 0 ? yv0 : yv1;
-        ptx::tma_load_2d_pair_hint(dst, &p.tm_kv, bar, x, yv, once);
-        ptx::tma_load_2d_pair_hint(dst + kChunkBytes, &p.tm_kv, bar, x + 64, yv, once);
+        ptx::tma_load_3d_pair_hint(dst, &p.tm_kv, bar, x, kvh, yv, once);
+        ptx::tma_load_3d_pair_hint(dst + kChunkBytes, &p.tm_kv, bar, x + 64, kvh, yv, once);
         ring.advance();
       }
     }
@@ -1271,20 +1293,20 @@ mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restr
 
 // ---------------------------------------------------------------------------
 // Plan of a ragged call (per-sequence KV lengths), one CTA: cu[v] = first tile of
-// virtual sequence v (batch x head groups + 1 entries) over lengths clamped to
-// [0, max_len]; sequences with no KV rows get out = 0 and lse = -inf here (the
-// decode kernel never visits them).
+// virtual sequence v (qb x head groups + 1 entries, qb query sequences of `heads`
+// rows) over the lengths qseq_len gives (seqlens nullptr: max_len for all); query
+// sequences with no KV rows get out = 0 and lse = -inf here (the decode kernel
+// never visits them).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024)
-mla_ragged_plan_kernel(const int* __restrict__ seqlens, int batch, int heads, int hgroups, int max_len,
-                       uint32_t* __restrict__ cu, void* __restrict__ out, float* __restrict__ lse,
+mla_ragged_plan_kernel(const int* __restrict__ seqlens, int qb, int heads, int hgroups, int q_len, int kv_heads,
+                       int max_len, uint32_t* __restrict__ cu, void* __restrict__ out, float* __restrict__ lse,
                        int out_elem_bytes) {
   __shared__ uint32_t s_part[1024];
   const int tid = threadIdx.x;
-  const int vb = batch * hgroups;
+  const int vb = qb * hgroups;
   auto tiles = [&](int v) -> uint32_t {
-    int len = seqlens[v / hgroups];
-    len = len < 0 ? 0 : (len > max_len ? max_len : len);
+    const int len = qseq_len(seqlens, v / hgroups, q_len, kv_heads, max_len);
     return (uint32_t)((len + kTile - 1) / kTile);
   };
   const int per = (vb + 1023) / 1024;
@@ -1305,8 +1327,8 @@ mla_ragged_plan_kernel(const int* __restrict__ seqlens, int batch, int heads, in
     run += tiles(v);
   }
   if (tid == 1023) cu[vb] = s_part[1023];
-  for (int row = tid; row < batch * heads; row += 1024) {
-    if (seqlens[row / heads] > 0 && max_len > 0) continue;
+  for (int row = tid; row < qb * heads; row += 1024) {
+    if (qseq_len(seqlens, row / heads, q_len, kv_heads, max_len) > 0) continue;
     uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(out) + (size_t)row * kDim * out_elem_bytes);
     for (int i = 0; i < kDim * out_elem_bytes / 16; ++i) o[i] = make_uint4(0u, 0u, 0u, 0u);
     if (lse != nullptr) lse[row] = -INFINITY;
@@ -1353,6 +1375,21 @@ bool make_map3(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, u
   const cuuint64_t dims[3] = {cols, rows, depth};
   const cuuint64_t strides[2] = {cols * elem_bytes, rows * cols * elem_bytes};
   const cuuint32_t box[3] = {128 / elem_bytes, 64, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// KV rows [rows][kv_heads][cols] (row-major), boxes of 64 rows x 1 KV head x 128
+// bytes, 128-byte swizzle: the smem tile of one KV head is the 2D 64 x 128-byte box.
+bool make_map_kv(CUtensorMap* m, const void* base, uint64_t cols, uint64_t kv_heads, uint64_t rows,
+                 CUtensorMapDataType dt) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[3] = {cols, kv_heads, rows};
+  const cuuint64_t strides[2] = {cols * 2, kv_heads * cols * 2};
+  const cuuint32_t box[3] = {64, 1, 64};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1417,14 +1454,29 @@ int current_max_pairs() {
 
 int head_groups(int heads) { return (heads + sm100::kHeads - 1) / sm100::kHeads; }
 
-bool sm100_supports(int batch, int heads, int seqlen_kv) {
+QShape qshape(const DecodeArgs& a) {
+  QShape s;
+  s.q_len = a.q_len > 0 ? a.q_len : 1;
+  s.kv_heads = a.kv_heads > 0 ? a.kv_heads : 1;
+  s.qb = a.batch * s.q_len * s.kv_heads;
+  s.g = a.heads / s.kv_heads;
+  s.hg = head_groups(s.g);
+  s.vb = s.qb * s.hg;
+  return s;
+}
+
+bool sm100_supports_ext(int batch, int q_len, int heads, int kv_heads, int seqlen_kv) {
   // 32-bit tile arithmetic in the kernel and int32 TMA row coordinates
-  if (heads < 1 || seqlen_kv < 1 || batch < 1) return false;
+  if (heads < 1 || seqlen_kv < 1 || batch < 1 || q_len < 1 || kv_heads < 1 || heads % kv_heads != 0)
+    return false;
   const long long nt = (seqlen_kv + sm100::kTile - 1) / sm100::kTile;
-  const long long vb = (long long)batch * head_groups(heads);
-  return vb * nt * (sm100::kMaxPairs + 1) < (1ll << 32) &&
+  const long long qb = (long long)batch * q_len * kv_heads;
+  const long long vb = qb * head_groups(heads / kv_heads);
+  return vb * nt * (sm100::kMaxPairs + 1) < (1ll << 32) && qb * heads < (1ll << 31) &&
          (long long)batch * seqlen_kv < (1ll << 31) - sm100::kTile;
 }
+
+bool sm100_supports(int batch, int heads, int seqlen_kv) { return sm100_supports_ext(batch, 1, heads, 1, seqlen_kv); }
 
 SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int* variant) {
   batch *= head_groups(heads);   // virtual sequences: one per (sequence, group of 128 heads)
@@ -1489,32 +1541,33 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
       a.dtype == MLA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const uint64_t kv_rows = a.block_table != nullptr ? (uint64_t)a.num_pages * a.page_size
                                                     : (uint64_t)a.batch * a.seqlen_kv;
-  if (!make_map(&p.tm_kv, a.kv, kDim, kv_rows, dt) || !make_map(&p.tm_kpe, a.k_pe, kPeDim, kv_rows, dt) ||
-      !make_map3(&p.tm_q, a.q, kDim, a.heads, a.batch, dt) ||
-      !make_map3(&p.tm_qpe, a.q_pe, kPeDim, a.heads, a.batch, dt))
+  const QShape qs = qshape(a);
+  if (!make_map_kv(&p.tm_kv, a.kv, kDim, qs.kv_heads, kv_rows, dt) ||
+      !make_map_kv(&p.tm_kpe, a.k_pe, kPeDim, qs.kv_heads, kv_rows, dt) ||
+      !make_map3(&p.tm_q, a.q, kDim, qs.g, qs.qb, dt) || !make_map3(&p.tm_qpe, a.q_pe, kPeDim, qs.g, qs.qb, dt))
     return cudaErrorInvalidValue;
   p.out_f32 = a.out_dtype == MLA_DTYPE_F32 ? 1 : 0;
   (void)variant;   // the combine launch (variant 1, ragged calls) takes what the kernel does not merge
   p.fuse_max = kFuseMaxPieces;
-  if (!(p.out_f32 ? make_map3(&p.tm_out, a.out, kDim, a.heads, a.batch, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4)
-                  : make_map3(&p.tm_out, a.out, kDim, a.heads, a.batch, dt)))
+  if (!(p.out_f32 ? make_map3(&p.tm_out, a.out, kDim, qs.g, qs.qb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4)
+                  : make_map3(&p.tm_out, a.out, kDim, qs.g, qs.qb, dt)))
     return cudaErrorInvalidValue;
   if (a.part_o != nullptr &&
       !make_map(&p.tm_part, a.part_o, kDim, (uint64_t)a.plan.part_rows, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4))
     return cudaErrorInvalidValue;
-  p.kv = static_cast<const uint8_t*>(a.kv);
   p.q = static_cast<const uint8_t*>(a.q);
   p.qpe = static_cast<const uint8_t*>(a.q_pe);
-  p.kpe = static_cast<const uint8_t*>(a.k_pe);
   p.out = a.out;
   p.lse_out = a.lse;
   p.part_o = a.part_o;
   p.part_lse = a.part_lse;
   p.status = a.status;
   p.counters = a.counters;
-  p.heads = a.heads;
-  p.hgroups = head_groups(a.heads);
-  p.batch = a.batch * p.hgroups;
+  p.heads = qs.g;
+  p.hgroups = qs.hg;
+  p.batch = qs.vb;
+  p.q_len = qs.q_len;
+  p.kv_heads = qs.kv_heads;
   p.seqlen = a.seqlen_kv;
   p.nt = (a.seqlen_kv + kTile - 1) / kTile;
   p.total_tiles = (uint32_t)p.batch * (uint32_t)p.nt;
@@ -1537,21 +1590,21 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
 cudaError_t launch_sm100_combine(const DecodeArgs& a) {
   using namespace sm100;
   const int nt = (a.seqlen_kv + kTile - 1) / kTile;
-  const int hg = head_groups(a.heads);
-  const int vb = a.batch * hg;
+  const QShape qs = qshape(a);
+  const int hg = qs.hg, vb = qs.vb;
   const uint32_t total = (uint32_t)vb * (uint32_t)nt;
   const dim3 grid(kHeads, vb);
   if (a.out_dtype == MLA_DTYPE_F32)
     mla_pair_combine_kernel<float><<<grid, 128, 0, a.stream>>>(
-        a.part_lse, a.part_o, static_cast<float*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb, a.heads,
+        a.part_lse, a.part_o, static_cast<float*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb, qs.g,
         hg, kFuseMaxPieces);
   else if (a.dtype == MLA_DTYPE_BF16)
     mla_pair_combine_kernel<__nv_bfloat16><<<grid, 128, 0, a.stream>>>(
         a.part_lse, a.part_o, static_cast<__nv_bfloat16*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb,
-        a.heads, hg, kFuseMaxPieces);
+        qs.g, hg, kFuseMaxPieces);
   else
     mla_pair_combine_kernel<__half><<<grid, 128, 0, a.stream>>>(
-        a.part_lse, a.part_o, static_cast<__half*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb, a.heads,
+        a.part_lse, a.part_o, static_cast<__half*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb, qs.g,
         hg, kFuseMaxPieces);
   return cudaGetLastError();
 }
@@ -1583,7 +1636,8 @@ cudaError_t launch_sm100_ragged_plan(const DecodeArgs& a) {
   const int elem = a.out_dtype == MLA_DTYPE_F32 ? 4 : 2;
   int cap = a.seqlen_kv;
   if (a.block_table != nullptr && (long long)a.max_pages * a.page_size < cap) cap = a.max_pages * a.page_size;
-  sm100::mla_ragged_plan_kernel<<<1, 1024, 0, a.stream>>>(a.seqlens, a.batch, a.heads, head_groups(a.heads),
+  const QShape qs = qshape(a);
+  sm100::mla_ragged_plan_kernel<<<1, 1024, 0, a.stream>>>(a.seqlens, qs.qb, qs.g, qs.hg, qs.q_len, qs.kv_heads,
                                                           cap, a.cu_tiles, a.out, a.lse, elem);
   return cudaGetLastError();
 }

@@ -8,8 +8,13 @@ namespace mla {
 // Groups of 128 heads per sequence: the tensor-core kernel's work units.
 int head_groups(int heads);
 
-// True when the tensor-core kernel covers this shape.
+// True when the tensor-core kernel covers this shape (q_len query positions per
+// sequence, heads query heads over kv_heads KV heads).
 bool sm100_supports(int batch, int heads, int seqlen_kv);
+bool sm100_supports_ext(int batch, int q_len, int heads, int kv_heads, int seqlen_kv);
+
+// Query-side shape the kernel sees for a call (DecodeArgs q_len / kv_heads).
+QShape qshape(const DecodeArgs& a);
 
 // Split plan (and kernel variant) the tensor-core kernel uses for this shape.
 SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int* variant);

@@ -207,21 +207,31 @@ def combine(part_lse: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor, lse
 
 
 class MlaPagedDecodeKernel:
-    """Decode over KV caches of different lengths, optionally paged.
+    """Decode over KV caches of different lengths, optionally paged, with
+    ``q_len`` query positions per sequence and ``kv_heads`` KV heads.
 
     ``kernel(q, q_pe, kv_cache, k_pe_cache, cache_seqlens, out, lse=None,
     block_table=None)``: ``cache_seqlens`` int32 [batch] gives each sequence's
-    KV rows (at most ``max_seqlen_kv``).  Without ``block_table`` the caches are
-    [batch, max_seqlen_kv, 1, 512] / [..., 64]; with it (int32 [batch,
-    max_pages]) they are pages [num_pages, page_size, 1, 512] / [..., 64] and
-    row r of sequence b is row r % page_size of page block_table[b, r //
-    page_size].  page_size is a multiple of 64.  No counterpart in the
-    reference (one kv_ctx per call there); the C entry point is
-    mla_decode_paged.
+    KV rows (at most ``max_seqlen_kv``), or None for all ``max_seqlen_kv``.
+    Without ``block_table`` the caches are [batch, max_seqlen_kv, kv_heads, 512]
+    / [..., 64]; with it (int32 [batch, max_pages]) they are pages [num_pages,
+    page_size, kv_heads, 512] / [..., 64] and row r of sequence b is row r %
+    page_size of page block_table[b, r // page_size].  page_size is a multiple
+    of 64.  q / out are [batch, heads, 512] for q_len == 1, else [batch, q_len,
+    heads, 512] (lse [batch, heads] / [batch, q_len, heads]); position t of a
+    sequence of L rows sees its first L - (q_len - 1 - t) rows.  Query head j
+    reads KV head j // (heads // kv_heads), as the reference's ref_program
+    groups them (baseline_mla.py:179-186).  No counterpart in the reference
+    (one kv_ctx, one query position and kv_heads == 1 per call there); the C
+    entry points are mla_decode_paged and mla_decode_ext.
     """
 
-    def __init__(self, batch, heads, max_seqlen_kv, cfg=None, softmax_scale=None):
+    def __init__(self, batch, heads, max_seqlen_kv, cfg=None, softmax_scale=None, q_len=1, kv_heads=1):
         self.batch, self.heads, self.max_seqlen_kv = int(batch), int(heads), int(max_seqlen_kv)
+        self.q_len, self.kv_heads = int(q_len), int(kv_heads)
+        if self.q_len < 1 or self.kv_heads < 1 or self.heads % self.kv_heads != 0:
+            raise ValueError(f"q_len and kv_heads must be >= 1 and divide heads (q_len {q_len}, heads {heads}, "
+                             f"kv_heads {kv_heads})")
         self.cfg = dict(cfg or {})
         if softmax_scale is not None:
             self.cfg["softmax_scale"] = float(softmax_scale)
@@ -231,7 +241,8 @@ class MlaPagedDecodeKernel:
         self._lock = threading.Lock()
 
     def workspace_bytes(self, dtype: torch.dtype) -> int:
-        return capi.paged_workspace_bytes(self.batch, self.heads, self.max_seqlen_kv, _DTYPES[dtype], self._ccfg)
+        return capi.ext_workspace_bytes(self.batch, self.q_len, self.heads, self.kv_heads, self.max_seqlen_kv,
+                                        _DTYPES[dtype], self._ccfg)
 
     def _workspace(self, device, dtype):
         key = (device.index, dtype)
@@ -253,25 +264,29 @@ class MlaPagedDecodeKernel:
         return int(ws[:4].view(torch.int32).item())
 
     def __call__(self, q, q_pe, kv_cache, k_pe_cache, cache_seqlens, out, lse=None, block_table=None):
-        b, h, smax = self.batch, self.heads, self.max_seqlen_kv
+        b, h, smax, ql, kvh = self.batch, self.heads, self.max_seqlen_kv, self.q_len, self.kv_heads
         dtype = q.dtype if isinstance(q, torch.Tensor) else None
         if dtype not in _DTYPES:
             raise ValueError(f"q must be float16 or bfloat16, got {dtype}")
         dev = q.device
-        _check_tensor("q", q, (b, h, DIM), dtype, None)
-        _check_tensor("q_pe", q_pe, (b, h, PE_DIM), dtype, dev)
-        _check_tensor("out", out, (b, h, DIM), dtype, dev)
-        _check_tensor("cache_seqlens", cache_seqlens, (b,), torch.int32, dev)
+        qshape = (b, h) if ql == 1 else (b, ql, h)
+        _check_tensor("q", q, (*qshape, DIM), dtype, None)
+        _check_tensor("q_pe", q_pe, (*qshape, PE_DIM), dtype, dev)
+        _check_tensor("out", out, (*qshape, DIM), dtype, dev)
+        sl_ptr = None
+        if cache_seqlens is not None:
+            _check_tensor("cache_seqlens", cache_seqlens, (b,), torch.int32, dev)
+            sl_ptr = cache_seqlens.data_ptr()
         if block_table is None:
-            _check_tensor("kv_cache", kv_cache, (b, smax, 1, DIM), dtype, dev)
-            _check_tensor("k_pe_cache", k_pe_cache, (b, smax, 1, PE_DIM), dtype, dev)
+            _check_tensor("kv_cache", kv_cache, (b, smax, kvh, DIM), dtype, dev)
+            _check_tensor("k_pe_cache", k_pe_cache, (b, smax, kvh, PE_DIM), dtype, dev)
             bt_ptr, page_size, num_pages, max_pages = None, 0, 0, 0
         else:
             if kv_cache.dim() != 4:
-                raise ValueError("kv_cache must be [num_pages, page_size, 1, 512]")
+                raise ValueError(f"kv_cache must be [num_pages, page_size, {kvh}, 512]")
             num_pages, page_size = int(kv_cache.shape[0]), int(kv_cache.shape[1])
-            _check_tensor("kv_cache", kv_cache, (num_pages, page_size, 1, DIM), dtype, dev)
-            _check_tensor("k_pe_cache", k_pe_cache, (num_pages, page_size, 1, PE_DIM), dtype, dev)
+            _check_tensor("kv_cache", kv_cache, (num_pages, page_size, kvh, DIM), dtype, dev)
+            _check_tensor("k_pe_cache", k_pe_cache, (num_pages, page_size, kvh, PE_DIM), dtype, dev)
             if block_table.dim() != 2 or block_table.shape[0] != b:
                 raise ValueError(f"block_table must be [batch, max_pages], got {tuple(block_table.shape)}")
             max_pages = int(block_table.shape[1])
@@ -279,11 +294,11 @@ class MlaPagedDecodeKernel:
             bt_ptr = block_table.data_ptr()
         lse_ptr = None
         if lse is not None:
-            _check_tensor("lse", lse, (b, h), torch.float32, dev)
+            _check_tensor("lse", lse, qshape, torch.float32, dev)
             lse_ptr = lse.data_ptr()
         ws = self._workspace(dev, dtype)
         with torch.cuda.device(dev):
             stream = torch.cuda.current_stream(dev).cuda_stream
-        capi.decode_paged(q.data_ptr(), q_pe.data_ptr(), kv_cache.data_ptr(), k_pe_cache.data_ptr(), bt_ptr,
-                          cache_seqlens.data_ptr(), out.data_ptr(), lse_ptr, ws.data_ptr(), ws.numel(), b, h, smax,
-                          page_size, num_pages, max_pages, _DTYPES[dtype], self._ccfg, stream)
+        capi.decode_ext(q.data_ptr(), q_pe.data_ptr(), kv_cache.data_ptr(), k_pe_cache.data_ptr(), bt_ptr, sl_ptr,
+                        out.data_ptr(), lse_ptr, ws.data_ptr(), ws.numel(), b, ql, h, kvh, smax, page_size,
+                        num_pages, max_pages, _DTYPES[dtype], self._ccfg, stream)

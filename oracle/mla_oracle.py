@@ -118,6 +118,69 @@ def ref_program_torch(q, q_pe, kv, k_pe):
     return out.permute(0, 2, 1, 3).reshape(b, -1, dim)
 
 
+def make_inputs_ext(batch, q_len, heads, kv_heads, seqlen_kv, dtype="bf16", seed=0, scale=1.0):
+    """Seeded host inputs with q_len query positions and kv_heads KV heads:
+    q[b,q_len,h,512], q_pe[b,q_len,h,64], kv[b,s,kv_heads,512], k_pe[b,s,kv_heads,64]
+    (same generator, draw order and casting as ``make_inputs``)."""
+    import torch
+
+    tdt = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32}[dtype]
+    g = torch.Generator().manual_seed(int(seed))
+    shapes = [(batch, q_len, heads, DIM), (batch, q_len, heads, PE_DIM),
+              (batch, seqlen_kv, kv_heads, DIM), (batch, seqlen_kv, kv_heads, PE_DIM)]
+    out = []
+    for shp in shapes:
+        x = torch.randn(*shp, generator=g, dtype=torch.float32)
+        if scale != 1.0:
+            x = x * scale
+        out.append(x.to(tdt))
+    return tuple(out)
+
+
+def ref_grouped_f64(q, q_pe, kv, k_pe):
+    """``ref_program`` (baseline_mla.py:177-191) for kv_head_num >= 1, exactly.
+
+    q[b,h,*], kv[b,s,kv_heads,*]: the reference rearranges q as
+    "b (h g) d -> b g h d" with g = heads // kv_heads (baseline_mla.py:179-182), so
+    query head j reads KV head j // g.  Returns (out[b,h,512], lse[b,h]) in float64.
+    """
+    kvh = kv.shape[2]
+    g = q.shape[1] // kvh
+    outs, lses = [], []
+    for i in range(kvh):
+        o, l = ref_program_f64(q[:, i * g:(i + 1) * g], q_pe[:, i * g:(i + 1) * g], kv[:, :, i:i + 1],
+                               k_pe[:, :, i:i + 1])
+        outs.append(o)
+        lses.append(l)
+    return np.concatenate(outs, axis=1), np.concatenate(lses, axis=1)
+
+
+def ref_multi_token_f64(q, q_pe, kv, k_pe, lens=None):
+    """Decode step of q_len query positions per sequence, causal within the step.
+
+    q[b,q_len,h,*], kv[b,s,kv_heads,*], lens[b] KV rows per sequence (None: s).
+    Position t of a sequence with L rows attends to its first L - (q_len - 1 - t)
+    rows (the step's new tokens are the cache's last q_len rows) with the
+    reference's grouped-head scores (``ref_grouped_f64``); a position with no rows
+    gives out = 0, lse = -inf.  The reference decodes one position per sequence
+    (baseline_mla.py:167-191); this extends it position by position.
+    Returns (out[b,q_len,h,512], lse[b,q_len,h]) in float64.
+    """
+    b, ql, h = q.shape[0], q.shape[1], q.shape[2]
+    s = kv.shape[1]
+    out = np.zeros((b, ql, h, DIM))
+    lse = np.full((b, ql, h), -np.inf)
+    for bb in range(b):
+        L = s if lens is None else max(0, min(int(lens[bb]), s))
+        for t in range(ql):
+            n = L - (ql - 1 - t)
+            if n <= 0:
+                continue
+            o, l = ref_grouped_f64(q[bb:bb + 1, t], q_pe[bb:bb + 1, t], kv[bb:bb + 1, :n], k_pe[bb:bb + 1, :n])
+            out[bb, t], lse[bb, t] = o[0], l[0]
+    return out, lse
+
+
 def split_plan(seqlen_kv, num_split, block_n, spread=False):
     """``_split_plan`` (mla_decode.py:9-30): -> (ns, blocks_per_cta, extra).
 

@@ -16,6 +16,12 @@ and writes:
   oracle).
 * ``split_plan.json`` -- ``_split_plan`` on a grid of (kv_ctx, num_split,
   block_N, spread), including the tail cases the reference documents.
+* ``ref_program_grouped.npz`` / ``ref_program_grouped_cases.json`` -- the same
+  for kv_head_num > 1 (``ref_program`` groups query heads over KV heads,
+  baseline_mla.py:179-189, although the reference's kernels assert
+  kv_head_num == 1), inputs from ``make_inputs_ext`` with q_len = 1.
+
+``--only grouped`` rewrites just the grouped files.
 
 Nothing on the GPU box runs this script: the fixtures it writes are committed.
 """
@@ -32,7 +38,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
-from oracle.mla_oracle import make_inputs  # noqa: E402
+from oracle.mla_oracle import make_inputs, make_inputs_ext  # noqa: E402
 
 # (name, dtype, batch, heads, kv_ctx, seed, scale)
 CASES = [
@@ -51,6 +57,14 @@ CASES = [
     ("h128_fp16_s1000_x0.1", "fp16", 1, 128, 1000, 11, 0.1),
 ]
 
+# (name, dtype, batch, heads, kv_heads, kv_ctx, seed): grouped KV heads
+GROUPED_CASES = [
+    ("grouped_bf16_b2_h128_kv2_s300", "bf16", 2, 128, 2, 300, 20),
+    ("grouped_fp16_b1_h64_kv4_s129", "fp16", 1, 64, 4, 129, 21),
+    ("grouped_bf16_b2_h32_kv8_s77", "bf16", 2, 32, 8, 77, 22),
+    ("grouped_bf16_b1_h256_kv2_s640", "bf16", 1, 256, 2, 640, 23),
+]
+
 # (kv_ctx, num_split, block_N, spread) grid for _split_plan.
 PLAN_CTX = [1, 7, 31, 32, 33, 63, 64, 65, 1000, 2048, 3000, 3008, 4095, 4096,
             8192, 16384, 32768, 65536, 131072]
@@ -62,14 +76,37 @@ def digest(t):
     return hashlib.sha256(t.contiguous().view(-1).view(__import__("torch").uint8).numpy().tobytes()).hexdigest()
 
 
+def gen_grouped(baseline_mla):
+    import torch
+
+    arrays, meta = {}, []
+    for name, dtype, b, h, kvh, s, seed in GROUPED_CASES:
+        q, q_pe, kv, k_pe = make_inputs_ext(b, 1, h, kvh, s, dtype, seed)
+        q, q_pe = q[:, 0].contiguous(), q_pe[:, 0].contiguous()
+        with torch.no_grad():
+            out64 = baseline_mla.ref_program(q.double(), q_pe.double(), kv.double(), k_pe.double())
+        arrays[f"{name}/out64"] = out64.float().numpy()
+        meta.append({"name": name, "dtype": dtype, "batch": b, "heads": h, "kv_heads": kvh, "kv_ctx": s,
+                     "seed": seed, "sha256": [digest(t) for t in (q, q_pe, kv, k_pe)]})
+    np.savez_compressed(os.path.join(HERE, "ref_program_grouped.npz"), **arrays)
+    with open(os.path.join(HERE, "ref_program_grouped_cases.json"), "w") as f:
+        json.dump(meta, f, indent=1)
+    print(f"wrote {len(meta)} grouped ref_program cases")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
+    ap.add_argument("--only", choices=["grouped"], default=None)
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.ref))
     import torch
     import baseline_mla  # the reference oracle
     import mla_decode    # the reference planner
+
+    gen_grouped(baseline_mla)
+    if args.only == "grouped":
+        return
 
     arrays = {}
     meta = []

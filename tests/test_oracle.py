@@ -112,3 +112,46 @@ def test_parity_gate_catches_planted_error():
     bad[0, 3] = 0.0
     assert not O.check_parity(bad, lse, ref, lse, "bf16")["ok"]
     assert not O.check_parity(good, lse + 2e-3, ref, lse, "bf16")["ok"]
+
+
+def _grouped_cases():
+    with open(os.path.join(GOLDEN, "ref_program_grouped_cases.json")) as f:
+        return json.load(f)
+
+
+@pytest.mark.parametrize("case", _grouped_cases(), ids=lambda c: c["name"])
+def test_grouped_oracle_matches_reference_ref_program(case):
+    """ref_grouped_f64 == baseline_mla.ref_program with kv_head_num > 1 (float64 inputs)."""
+    golden = np.load(os.path.join(GOLDEN, "ref_program_grouped.npz"))
+    q, q_pe, kv, k_pe = O.make_inputs_ext(case["batch"], 1, case["heads"], case["kv_heads"], case["kv_ctx"],
+                                          case["dtype"], case["seed"])
+    q, q_pe = q[:, 0].contiguous(), q_pe[:, 0].contiguous()
+    assert [_digest(x) for x in (q, q_pe, kv, k_pe)] == case["sha256"]
+    out, lse = O.ref_grouped_f64(q, q_pe, kv, k_pe)
+    ref = golden[f"{case['name']}/out64"].astype(np.float64)
+    assert np.abs(out - ref).max() <= 1e-6 * max(1.0, np.abs(ref).max())
+    # the grouped torch restatement (the CPU baseline) follows the same grouping
+    tout = O.ref_program_torch(q.double(), q_pe.double(), kv.double(), k_pe.double()).numpy()
+    assert np.abs(tout - ref).max() <= 1e-6 * max(1.0, np.abs(ref).max())
+
+
+def test_multi_token_oracle_follows_the_causal_rule():
+    """Position t of a q_len-token step equals the one-token reference on the first
+    L - (q_len - 1 - t) rows; q_len = 1 is the plain reference; empty positions are 0 / -inf."""
+    b, ql, h, kvh, s = 3, 3, 32, 2, 70
+    q, q_pe, kv, k_pe = O.make_inputs_ext(b, ql, h, kvh, s, "bf16", seed=31)
+    lens = [70, 2, 40]
+    out, lse = O.ref_multi_token_f64(q, q_pe, kv, k_pe, lens)
+    for bb, L in enumerate(lens):
+        for t in range(ql):
+            n = L - (ql - 1 - t)
+            if n <= 0:
+                assert np.all(out[bb, t] == 0) and np.all(np.isneginf(lse[bb, t]))
+                continue
+            o, l = O.ref_grouped_f64(q[bb:bb + 1, t], q_pe[bb:bb + 1, t], kv[bb:bb + 1, :n], k_pe[bb:bb + 1, :n])
+            np.testing.assert_allclose(out[bb, t], o[0], rtol=0, atol=1e-12)
+            np.testing.assert_allclose(lse[bb, t], l[0], rtol=0, atol=1e-12)
+    one, one_lse = O.ref_multi_token_f64(q[:, -1:], q_pe[:, -1:], kv, k_pe, None)
+    o, l = O.ref_grouped_f64(q[:, -1], q_pe[:, -1], kv, k_pe)
+    np.testing.assert_allclose(one[:, 0], o, rtol=0, atol=1e-12)
+    np.testing.assert_allclose(one_lse[:, 0], l, rtol=0, atol=1e-12)
