@@ -42,21 +42,30 @@ class MlaDecodeKernel:
 
     ``cfg`` is a reference-style config dict (keys block_N, block_H, num_split,
     spread, num_stages, combine_groups; plus ``kernel`` = "auto"/"simt"/"tc"),
-    or None to let the library choose.  Only the absorbed shape of the
-    reference is accepted: kv_heads == 1, dim == 512, pe_dim == 64
-    (baseline_mla.py:16).
+    or None to let the library choose.  dim == 512 and pe_dim == 64.  The
+    reference's kernels take kv_heads == 1 only (mla_decode.py:16); here
+    kv_head_num > 1 (heads a multiple of it, kv [batch, kv_ctx, kv_head_num,
+    512]) runs through mla_decode_ext with the reference ref_program's head
+    grouping, for ``__call__`` only.
     """
 
     def __init__(self, batch, heads, kv_head_num, seqlen_kv, dim=DIM, pe_dim=PE_DIM, cfg=None,
                  softmax_scale=None):
-        if int(kv_head_num) != 1:
-            raise ValueError(f"kv_head_num must be 1 (absorbed MLA), got {kv_head_num}")
+        kvh = int(kv_head_num)
+        if kvh < 1 or int(heads) % kvh != 0:
+            raise ValueError(f"kv_head_num must be >= 1 and divide heads, got {kv_head_num} for {heads} heads")
+        self._grouped = None
+        if kvh > 1:
+            if (cfg or {}).get("kernel", "auto") == "simt":
+                raise ValueError("kv_head_num > 1 runs on the tensor-core kernel only")
+            self._grouped = MlaPagedDecodeKernel(batch, heads, seqlen_kv, cfg=cfg, softmax_scale=softmax_scale,
+                                                 kv_heads=kvh)
         if int(dim) != DIM or int(pe_dim) != PE_DIM:
             raise ValueError(f"dim/pe_dim must be {DIM}/{PE_DIM}, got {dim}/{pe_dim}")
         if int(batch) < 1 or int(heads) < 1 or int(seqlen_kv) < 1:
             raise ValueError("batch, heads and seqlen_kv must be >= 1")
         self.batch, self.heads, self.seqlen_kv = int(batch), int(heads), int(seqlen_kv)
-        self.kv_heads, self.dim, self.pe_dim = 1, DIM, PE_DIM
+        self.kv_heads, self.dim, self.pe_dim = kvh, DIM, PE_DIM
         self.cfg = dict(cfg or {})
         if softmax_scale is not None:
             self.cfg["softmax_scale"] = float(softmax_scale)
@@ -67,7 +76,13 @@ class MlaDecodeKernel:
 
     # -- workspace ---------------------------------------------------------
     def workspace_bytes(self, dtype: torch.dtype) -> int:
+        if self._grouped is not None:
+            return self._grouped.workspace_bytes(dtype)
         return capi.workspace_bytes(self.batch, self.heads, self.seqlen_kv, _DTYPES[dtype], self._ccfg)
+
+    def _one_kv_head(self, what):
+        if self._grouped is not None:
+            raise NotImplementedError(f"{what} takes kv_head_num == 1 (this kernel has {self.kv_heads})")
 
     def _workspace(self, device, dtype):
         key = (device.index, dtype)
@@ -89,6 +104,9 @@ class MlaDecodeKernel:
         ``lse`` (optional, float32 [batch, heads]) receives the natural-log
         log-sum-exp of the scaled scores.
         """
+        if self._grouped is not None:
+            self._grouped(q, q_pe, kv, k_pe, None, out, lse)
+            return
         b, h, s = self.batch, self.heads, self.seqlen_kv
         dtype = q.dtype if isinstance(q, torch.Tensor) else None
         if dtype not in _DTYPES:
@@ -116,6 +134,7 @@ class MlaDecodeKernel:
         ``lse`` float32 [batch, heads] the natural-log log-sum-exp; results of
         several parts of the same sequences merge with :func:`combine`.
         """
+        self._one_kv_head("partial")
         b, h, s = self.batch, self.heads, self.seqlen_kv
         dtype = q.dtype if isinstance(q, torch.Tensor) else None
         if dtype not in _DTYPES:
@@ -139,6 +158,7 @@ class MlaDecodeKernel:
 
         Device pointers and shapes are trusted to match a previous checked call.
         """
+        self._one_kv_head("splitkv")
         ws = self._workspace(q.device, q.dtype)
         stream = torch.cuda.current_stream(q.device).cuda_stream
         capi.decode_splitkv(q.data_ptr(), q_pe.data_ptr(), kv.data_ptr(), k_pe.data_ptr(), out.data_ptr(),
@@ -147,6 +167,7 @@ class MlaDecodeKernel:
 
     def combine_ws(self, out, lse=None):
         """Second launch of a call: combine the partials ``splitkv`` left in the workspace."""
+        self._one_kv_head("combine_ws")
         ws = self._workspace(out.device, out.dtype)
         stream = torch.cuda.current_stream(out.device).cuda_stream
         capi.decode_combine_ws(out.data_ptr(), None if lse is None else lse.data_ptr(), ws.data_ptr(),
@@ -155,6 +176,8 @@ class MlaDecodeKernel:
 
     def device_status(self, device, dtype) -> int:
         """Status word the tensor-core kernel leaves in the workspace (0 = no timeout)."""
+        if self._grouped is not None:
+            return self._grouped.device_status(device, dtype)
         ws = self._ws.get((torch.device(device).index, dtype))
         if ws is None or ws.numel() < 4:
             return 0
@@ -162,6 +185,7 @@ class MlaDecodeKernel:
 
     def plan(self, dtype=torch.bfloat16) -> dict:
         """The library's plan for this shape: kernel, splits/pairs, launches per call."""
+        self._one_kv_head("plan")
         return capi.describe_plan(self.batch, self.heads, self.seqlen_kv, _DTYPES[dtype], self._ccfg)
 
     def launches_per_call(self, dtype=torch.bfloat16) -> int:

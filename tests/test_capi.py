@@ -129,6 +129,11 @@ def test_kernel_object_rejects_non_absorbed_shapes():
     from mlc_decode_b200 import MlaDecodeKernel
 
     with pytest.raises(ValueError):
-        MlaDecodeKernel(1, 16, 2, 64, 512, 64)
+        MlaDecodeKernel(1, 16, 3, 64, 512, 64)    # heads not a multiple of kv_head_num
+    with pytest.raises(ValueError):
+        MlaDecodeKernel(1, 16, 2, 64, 512, 64, cfg={"kernel": "simt"})
     with pytest.raises(ValueError):
         MlaDecodeKernel(1, 16, 1, 64, 256, 64)
+    k = MlaDecodeKernel(1, 16, 2, 64, 512, 64)   # grouped KV heads: the mla_decode_ext path
+    with pytest.raises(NotImplementedError):
+        k.plan()

@@ -122,6 +122,23 @@ def test_multi_token_grouped_paged(cuda):
     _check(out, lse, ref, ref_lse, "bf16")
 
 
+def test_dropin_factory_grouped_kv_heads(cuda):
+    """MlaDecodeKernel(batch, heads, kv_head_num > 1, kv_ctx) as the reference factory is called."""
+    from mlc_decode_b200 import MlaDecodeKernel
+
+    b, h, kvh, s = 2, 64, 4, 1000
+    q, qp, kv, kp = O.make_inputs_ext(b, 1, h, kvh, s, "bf16", seed=47)
+    q, qp = q[:, 0].contiguous(), qp[:, 0].contiguous()
+    ref, ref_lse = O.ref_grouped_f64(q, qp, kv, kp)
+    dev = "cuda"
+    out = torch.empty(b, h, 512, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(b, h, device=dev)
+    MlaDecodeKernel(b, h, kvh, s)(q.to(dev), qp.to(dev), kv.to(dev), kp.to(dev), out, lse)
+    torch.cuda.synchronize()
+    res = O.check_parity(out.float().cpu().numpy(), lse.cpu().numpy(), ref, ref_lse, "bf16")
+    assert res["ok"], res
+
+
 def test_ext_rejects_bad_grouping(cuda):
     from mlc_decode_b200 import MlaPagedDecodeKernel
 
