@@ -177,6 +177,24 @@ int32_t mla_decode_partial(const void* q, const void* q_pe, const void* kv,
                            int32_t dtype, const MlaCfg* cfg, void* stream);
 
 /*
+ * mla_decode_fwd over an FP8 latent KV cache: kv_fp8 [batch, seqlen_kv, 1, 512]
+ * holds e4m3 (OCP FP8, 4 exponent / 3 mantissa bits, one byte per dim) values
+ * whose product with kv_scale is the latent row; q, q_pe, k_pe and out stay in
+ * `dtype`.  Half the latent bytes of mla_decode_fwd.  The latent rows are
+ * dequantized to fp16 in shared memory (exact), Q's latent dims are rounded to
+ * fp16 after multiplying by kv_scale (|q| x kv_scale must stay within fp16
+ * range), P is fp16, accumulation fp32.  Tensor-core kernel only (cfg->kernel
+ * auto or tc); workspace as mla_workspace_bytes(batch, heads, seqlen_kv, dtype,
+ * cfg) reports for the same cfg.  No counterpart in the reference (listed as
+ * untried in its notes, docs/mla_decode_best_implementation.md:1693).
+ */
+int32_t mla_decode_fp8kv(const void* q, const void* q_pe, const void* kv_fp8,
+                         const void* k_pe, float kv_scale, void* out, float* lse,
+                         void* workspace, size_t workspace_bytes,
+                         int32_t batch, int32_t heads, int32_t seqlen_kv,
+                         int32_t dtype, const MlaCfg* cfg, void* stream);
+
+/*
  * Decode over KV caches of different lengths, optionally paged (the caller-side
  * format of serving decode).  No counterpart in the reference, whose kernel takes
  * one kv_ctx for the whole batch (its design notes name per-sequence lengths as

@@ -293,6 +293,35 @@ int32_t mla_decode_fwd(const void* q, const void* q_pe, const void* kv, const vo
   return run_combine_ws("mla_decode_fwd", a, r);
 }
 
+int32_t mla_decode_fp8kv(const void* q, const void* q_pe, const void* kv_fp8, const void* k_pe,
+                         float kv_scale, void* out, float* lse, void* workspace, size_t workspace_bytes,
+                         int32_t batch, int32_t heads, int32_t seqlen_kv, int32_t dtype, const MlaCfg* cfg,
+                         void* stream) {
+  const char* fn = "mla_decode_fp8kv";
+  MlaCfg c{};
+  if (cfg != nullptr) c = *cfg;
+  if (c.kernel == MLA_KERNEL_SIMT) {
+    set_error("%s: runs on the tensor-core kernel only (kernel = auto or tc)", fn);
+    return MLA_ERR_UNSUPPORTED;
+  }
+  c.kernel = MLA_KERNEL_TC;
+  if (!(kv_scale > 0.f) || !isfinite(kv_scale)) {
+    set_error("%s: kv_scale must be finite and > 0", fn);
+    return MLA_ERR_ARG;
+  }
+  DecodeArgs a;
+  Resolved r;
+  size_t need = 0;
+  int rc = prepare(fn, q, q_pe, kv_fp8, k_pe, out, lse, workspace, workspace_bytes, batch, heads, seqlen_kv,
+                   dtype, &c, stream, true, &a, &r, &need);
+  if (rc != MLA_OK) return rc;
+  a.kv_fp8 = 1;
+  a.kv_scale = kv_scale;
+  rc = run_splitkv(fn, a, r);
+  if (rc != MLA_OK) return rc;
+  return run_combine_ws(fn, a, r);
+}
+
 int32_t mla_decode_partial(const void* q, const void* q_pe, const void* kv, const void* k_pe,
                            float* o, float* lse, void* workspace, size_t workspace_bytes,
                            int32_t batch, int32_t heads, int32_t seqlen_kv, int32_t dtype,

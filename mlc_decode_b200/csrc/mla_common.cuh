@@ -126,6 +126,10 @@ struct DecodeArgs {
   // heads [i*h/kv_heads, (i+1)*h/kv_heads) read KV head i); 0 means 1.
   // Tensor-core kernel only.
   int q_len, kv_heads;
+  // kv holds e4m3 latent rows (one byte per dim) to be multiplied by kv_scale
+  // (tensor-core kernel only); k_pe stays in `dtype`
+  int kv_fp8;
+  float kv_scale;
   float softmax_scale;  // multiplies raw scores
   SplitPlan plan;
   cudaStream_t stream;

@@ -39,6 +39,7 @@
 //    pair raises an abort flag, records a status code in the workspace and
 //    winds down (no trap, no hang).
 #include <cuda.h>
+#include <cuda_fp8.h>
 #include <cudaTypedefs.h>
 #include <math.h>
 
@@ -63,12 +64,12 @@ constexpr uint32_t kPBytes = 2 * kChunkBytes;   // one P operand: 64 rows x 128 
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 128;
 constexpr uint32_t kColQT = 384;      // Q dims [0, 256) as bf16/fp16 pairs: 128 columns
-constexpr int kThreads = 384;       // 3 warpgroups
-// Registers per thread after the split: launch budget 384 x 168; producers,
-// issuers and the Q loader need few, the softmax warps many
-// (2 x 128 x kRegsLow + 128 x kRegsSoftmax <= 384 x 168).
+// Registers per thread after the split: launch budget 384 x 168 (512 x 128 for
+// the FP8 variant's 4 warpgroups); producers, issuers, the Q loader and the
+// converters need few, the softmax warps many.
 constexpr uint32_t kRegsLow = 88, kRegsSoftmax = 232;
 static_assert(2 * 128 * kRegsLow + 128 * kRegsSoftmax <= 384 * 168, "register split");
+static_assert(3 * 128 * kRegsLow + 128 * kRegsSoftmax <= 512 * 128, "register split (FP8 variant)");
 constexpr float kRescaleLog2 = 8.0f;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr int kMaxPairs = 256;        // CTA pairs per launch (schedule bound)
@@ -90,21 +91,63 @@ struct Cfg;
 template <>
 struct Cfg<__nv_bfloat16> {
   static constexpr uint32_t kFmt = 1;
+  static constexpr uint32_t kRopeFmt = 1;
   static constexpr int kPParts = 2;
   static constexpr int kKStages = 4;
   static constexpr int kVStages = 3;
+  static constexpr int kK8Stages = 0;
+  static constexpr int kV8Stages = 0;
+  using PT = __nv_bfloat16;   // P operand type
 };
 template <>
 struct Cfg<__half> {
   static constexpr uint32_t kFmt = 0;
+  static constexpr uint32_t kRopeFmt = 0;
   static constexpr int kPParts = 1;
   static constexpr int kKStages = 6;
   static constexpr int kVStages = 3;
+  static constexpr int kK8Stages = 0;
+  static constexpr int kV8Stages = 0;
+  using PT = __half;
 };
+
+// The FP8 variant: latent KV rows in e4m3 (one byte per dim), dequantized to fp16
+// in shared memory by converter warps; every latent MMA and P run in fp16 (e4m3 ->
+// fp16 is exact; fp16 P needs no hi/lo pair).  T is the type of q, q_pe, k_pe
+// and out; the rope MMAs stay in T.  The tensor's scale is folded into Q's latent
+// dims (once per piece) and into the output normalisation.
+template <typename T>
+struct Kv8 {};
+template <typename K>
+struct Io {
+  using Out = K;
+  static constexpr bool kKv8 = false;
+};
+template <typename T>
+struct Io<Kv8<T>> {
+  using Out = T;
+  static constexpr bool kKv8 = true;
+};
+template <typename T>
+struct Cfg<Kv8<T>> {
+  static constexpr uint32_t kFmt = 0;
+  static constexpr uint32_t kRopeFmt = Cfg<T>::kFmt;
+  static constexpr int kPParts = 1;
+  static constexpr int kKStages = 3;    // fp16 operand stages (16 KB)
+  static constexpr int kVStages = 2;
+  static constexpr int kK8Stages = 4;   // e4m3 (or rope) stages as loaded (8 KB)
+  static constexpr int kV8Stages = 4;
+  using PT = __half;
+};
+template <typename K>
+constexpr int threads_of() { return Io<K>::kKv8 ? 512 : 384; }
 
 struct Barriers {
   uint64_t kfull[8], kempty[8];
   uint64_t vfull[8], vempty[8];
+  uint64_t k8full[4], k8empty[4];   // FP8 variant: e4m3 stages as loaded
+  uint64_t v8full[4], v8empty[4];
+  uint64_t qsm;                     // FP8 variant: this CTA's Q rows in shared memory
   uint64_t q_full, q_empty, qt_full;
   uint64_t s_full[2], s_free[2];
   uint64_t p_full[2];
@@ -114,7 +157,7 @@ struct Barriers {
   uint64_t q_go;         // the first piece's Q loads are issued: K and V loads may start
   uint64_t drain_qk, drain_pv;
 };
-static_assert(sizeof(Barriers) <= 512, "barrier block");
+static_assert(sizeof(Barriers) <= 1024, "barrier block");
 
 // shared memory map (offsets from the 1024-byte aligned base)
 template <typename T>
@@ -124,8 +167,10 @@ struct Smem {
   static constexpr uint32_t kPBuf = Cfg<T>::kPParts * kPBytes;     // one P buffer (hi [, lo])
   static constexpr uint32_t kKRing = kP + 2 * kPBuf;
   static constexpr uint32_t kVRing = kKRing + Cfg<T>::kKStages * kStageBytes;
-  static constexpr uint32_t kBar = kVRing + Cfg<T>::kVStages * kStageBytes;
-  static constexpr uint32_t kXmax = kBar + 512;
+  static constexpr uint32_t kK8Ring = kVRing + Cfg<T>::kVStages * kStageBytes;
+  static constexpr uint32_t kV8Ring = kK8Ring + Cfg<T>::kK8Stages * kChunkBytes;
+  static constexpr uint32_t kBar = kV8Ring + Cfg<T>::kV8Stages * kChunkBytes;
+  static constexpr uint32_t kXmax = kBar + 1024;
   static constexpr uint32_t kXl = kXmax + 2 * 128 * 4;
   static constexpr uint32_t kMisc = kXl + 128 * 4;
   static constexpr uint32_t kBytes = kMisc + 64 + 1024;   // + alignment slack
@@ -133,7 +178,7 @@ struct Smem {
 };
 
 struct Params {
-  CUtensorMap tm_kv;    // [b*s][kv_heads][512], box 64 x 1 x 64 rows
+  CUtensorMap tm_kv;    // [b*s][kv_heads][512], box 64 x 1 x 64 rows (e4m3: 128 x 1 x 64)
   CUtensorMap tm_kpe;   // [b*s][kv_heads][64]
   CUtensorMap tm_q;     // [qb][h][512], box 64 x 64 x 1 (rows past h read as zero)
   CUtensorMap tm_qpe;   // [qb][h][64]
@@ -147,6 +192,7 @@ struct Params {
   float* part_lse;
   uint32_t* status;
   uint32_t* counters;   // [batch][2] pieces finished per (sequence, CTA rank); zero between calls
+  float kv_scale;       // FP8 variant: dequantisation scale of the e4m3 latent rows
   // Work units are "virtual sequences".  The query side is qb = b x q_len x
   // kv_heads query sequences qs = (s * q_len + t) * kv_heads + kvh (query
   // position t of sequence s, the query heads of KV head kvh: rows of q/out
@@ -369,6 +415,33 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
   const uint64_t keep = ptx::l2_policy_evict_last();
   const uint64_t once = ptx::l2_policy_evict_first();
   Piece pc;
+  if constexpr (Io<T>::kKv8) {
+    // FP8: this CTA's e4m3 latent units (64 rows x 128 dims, 8 KB) and its rope
+    // unit into the e4m3 ring, each on a local barrier; the converter warps turn
+    // them into the fp16 operand ring
+    const uint32_t k8full0 = ptx::smem_u32(&bars->k8full[0]);
+    const uint32_t k8empty0 = ptx::smem_u32(&bars->k8empty[0]);
+    Ring<Cfg<T>::kK8Stages> r8;
+    while (it.next(&pc)) {
+      const int kseq = vseq_kvseq(p, pc.bb), kvh = vseq_kvh(p, pc.bb), klen = seq_len(p, pc.bb);
+#pragma unroll 1
+      for (int j = pc.first; j < pc.end; ++j) {
+        const int y = kv_row(p, kseq, j * kTile + 64 * (int)rank, klen);
+#pragma unroll 1
+        for (int u = 0; u < 5; ++u) {
+          if (!wait_bar(c, k8empty0 + 8 * r8.stage, r8.phase ^ 1u, kErrKLoad)) return;
+          const uint32_t bar = k8full0 + 8 * r8.stage;
+          const uint32_t dst = sbase + S::kK8Ring + r8.stage * kChunkBytes;
+          ptx::mbar_arrive_expect_tx(bar, kChunkBytes);
+          if (u < 4)
+            ptx::tma_load_3d_local_hint(dst, &p.tm_kv, bar, 128 * u, kvh, y, keep);
+          else
+            ptx::tma_load_3d_local_hint(dst, &p.tm_kpe, bar, 0, kvh, y, once);
+          r8.advance();
+        }
+      }
+    }
+  } else {
   // K units stream straight across piece boundaries: Q has its own loader thread
   while (it.next(&pc)) {
     const int kseq = vseq_kvseq(p, pc.bb), kvh = vseq_kvh(p, pc.bb), klen = seq_len(p, pc.bb);
@@ -391,6 +464,7 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
         ring.advance();
       }
     }
+  }
   }
 }
 
@@ -445,12 +519,23 @@ __device__ __forceinline__ void q_loader(const Params& p, const Ctx& c, uint32_t
     for (int ch = 0; ch < 4; ++ch)
       ptx::tma_load_3d_local(qt_dst + ch * kChunkBytes, &p.tm_q, qts, 64 * ch, qrow, qseq);
     if (piece > 0 && !wait_bar(c, qtr, (uint32_t)piece & 1u, kErrKLoad)) return;
-    if (leader) ptx::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
+    if constexpr (Io<T>::kKv8) {
+      // FP8: local loads; the softmax warps convert the latent dims to scaled fp16
+      // in place before they release the piece's Q to the QK^T issuer
+      const uint32_t qsm = ptx::smem_u32(&bars->qsm);
+      ptx::mbar_arrive_expect_tx(qsm, kQBytes);
 #pragma unroll 1
-    for (int ch = 0; ch < 4; ++ch)
-      ptx::tma_load_3d_pair(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, q_full_leader, kQTDims + 64 * ch,
-                            qrow, qseq);
-    ptx::tma_load_3d_pair(sbase + S::kQ + 4 * kChunkBytes, &p.tm_qpe, q_full_leader, 0, qrow, qseq);
+      for (int ch = 0; ch < 4; ++ch)
+        ptx::tma_load_3d_local(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, qsm, kQTDims + 64 * ch, qrow, qseq);
+      ptx::tma_load_3d_local(sbase + S::kQ + 4 * kChunkBytes, &p.tm_qpe, qsm, 0, qrow, qseq);
+    } else {
+      if (leader) ptx::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
+#pragma unroll 1
+      for (int ch = 0; ch < 4; ++ch)
+        ptx::tma_load_3d_pair(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, q_full_leader, kQTDims + 64 * ch,
+                              qrow, qseq);
+      ptx::tma_load_3d_pair(sbase + S::kQ + 4 * kChunkBytes, &p.tm_qpe, q_full_leader, 0, qrow, qseq);
+    }
     if (piece == 0) ptx::mbar_arrive_local(q_go);
     ++piece;
   }
@@ -474,6 +559,30 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
   PieceIter it(p, pair);
   if (!wait_bar(c, ptx::smem_u32(&bars->q_go), 0u, kErrVLoad)) return;
   Piece pc;
+  if constexpr (Io<T>::kKv8) {
+    // FP8: unit u = (nh, th) is this CTA's 128 latent dims [256 nh + 128 rank, +128)
+    // of tokens [64 th, +64) in e4m3 (one 8 KB box), on a local barrier
+    const uint32_t v8full0 = ptx::smem_u32(&bars->v8full[0]);
+    const uint32_t v8empty0 = ptx::smem_u32(&bars->v8empty[0]);
+    Ring<Cfg<T>::kV8Stages> r8;
+    while (it.next(&pc)) {
+      const int vseq = vseq_kvseq(p, pc.bb), kvh = vseq_kvh(p, pc.bb), vlen = seq_len(p, pc.bb);
+#pragma unroll 1
+      for (int j = pc.first; j < pc.end; ++j) {
+        const int yv0 = kv_row(p, vseq, j * kTile, vlen), yv1 = kv_row(p, vseq, j * kTile + 64, vlen);
+#pragma unroll 1
+        for (int u = 0; u < 4; ++u) {
+          const int nh = u >> 1, th = u & 1;
+          if (!wait_bar(c, v8empty0 + 8 * r8.stage, r8.phase ^ 1u, kErrVLoad)) return;
+          const uint32_t bar = v8full0 + 8 * r8.stage;
+          ptx::mbar_arrive_expect_tx(bar, kChunkBytes);
+          ptx::tma_load_3d_local_hint(sbase + S::kV8Ring + r8.stage * kChunkBytes, &p.tm_kv, bar,
+                                      256 * nh + 128 * (int)rank, kvh, th == 0 ? yv0 : yv1, once);
+          r8.advance();
+        }
+      }
+    }
+  } else {
   while (it.next(&pc)) {
     const int vseq = vseq_kvseq(p, pc.bb), kvh = vseq_kvh(p, pc.bb), vlen = seq_len(p, pc.bb);
 #pragma unroll 1
@@ -496,6 +605,85 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
       }
     }
   }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// FP8 variant: converter warps.  Two warps per side (K: latent units + the rope
+// unit of each tile; V: the four units of each tile) take an e4m3 stage (64 rows x
+// 128 dims, one SW128 box) and write the fp16 operand stage the MMAs read (the same
+// rows as two SW128 boxes of 64 dims), then release the e4m3 stage (local) and
+// signal the operand stage to the even CTA's issuer (count 2 warps x 2 CTAs).
+// e4m3 -> fp16 is exact.  The rope unit is copied as loaded (already in the
+// operand layout).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t v) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(v & 0xffffu), __NV_E4M3);
+  return (uint32_t)h.x | ((uint32_t)h.y << 16);
+}
+
+template <typename T>
+__device__ __forceinline__ void converter(const Params& p, const Ctx& c, int pair, uint8_t* smem,
+                                          Barriers* bars, bool kside, int ct, int lane) {
+  using S = Smem<T>;
+  const uint32_t full8 = ptx::smem_u32(kside ? &bars->k8full[0] : &bars->v8full[0]);
+  const uint32_t empty8 = ptx::smem_u32(kside ? &bars->k8empty[0] : &bars->v8empty[0]);
+  const uint32_t op_empty = ptx::smem_u32(kside ? &bars->kempty[0] : &bars->vempty[0]);
+  const uint32_t op_full_leader = ptx::mapa(ptx::smem_u32(kside ? &bars->kfull[0] : &bars->vfull[0]), 0);
+  const uint8_t* ring8 = smem + (kside ? S::kK8Ring : S::kV8Ring);
+  uint8_t* ring_op = smem + (kside ? S::kKRing : S::kVRing);
+  const uint32_t n8 = kside ? Cfg<T>::kK8Stages : Cfg<T>::kV8Stages;
+  const uint32_t n_op = kside ? Cfg<T>::kKStages : Cfg<T>::kVStages;
+  const int units = kside ? 5 : 4;
+  const uint32_t code = kside ? kErrKLoad : kErrVLoad;
+  uint32_t s8 = 0, ph8 = 0, so = 0, pho = 0;
+  PieceIter it(p, pair);
+  Piece pc;
+  while (it.next(&pc)) {
+#pragma unroll 1
+    for (int j = pc.first; j < pc.end; ++j) {
+#pragma unroll 1
+      for (int u = 0; u < units; ++u) {
+        if (!wait_bar(c, full8 + 8 * s8, ph8, code)) return;
+        if (!wait_bar(c, op_empty + 8 * so, pho ^ 1u, code)) return;
+        const uint8_t* src = ring8 + s8 * kChunkBytes;
+        uint8_t* dst = ring_op + so * kStageBytes;
+        if (kside && u == 4) {
+#pragma unroll
+          for (int i = ct; i < 512; i += 64)
+            *reinterpret_cast<uint4*>(dst + 16 * i) = *reinterpret_cast<const uint4*>(src + 16 * i);
+        } else {
+#pragma unroll 4
+          for (int i = ct; i < 512; i += 64) {
+            // logical 16-byte granule g of row r (elements [16 g, 16 g + 16)) sits at g ^ (r & 7)
+            const int r = i >> 3, g = i & 7;
+            const uint4 x = *reinterpret_cast<const uint4*>(src + r * 128 + ((g ^ (r & 7)) << 4));
+            uint8_t* row = dst + (g >> 2) * kChunkBytes + r * 128;
+            const int g1 = 2 * (g & 3);
+            *reinterpret_cast<uint4*>(row + ((g1 ^ (r & 7)) << 4)) =
+                make_uint4(e4m3x2_to_h2(x.x), e4m3x2_to_h2(x.x >> 16), e4m3x2_to_h2(x.y), e4m3x2_to_h2(x.y >> 16));
+            *reinterpret_cast<uint4*>(row + (((g1 + 1) ^ (r & 7)) << 4)) =
+                make_uint4(e4m3x2_to_h2(x.z), e4m3x2_to_h2(x.z >> 16), e4m3x2_to_h2(x.w), e4m3x2_to_h2(x.w >> 16));
+          }
+        }
+        // the tensor core reads the stage through the async proxy
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::mbar_arrive_local(empty8 + 8 * s8);
+          ptx::mbar_arrive_cluster(op_full_leader + 8 * so);
+        }
+        if (++s8 == n8) {
+          s8 = 0;
+          ph8 ^= 1u;
+        }
+        if (++so == n_op) {
+          so = 0;
+          pho ^= 1u;
+        }
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -507,6 +695,7 @@ __device__ __forceinline__ void qk_issuer(const Params& p, const Ctx& c, int pai
   using S = Smem<T>;
   constexpr int KS = Cfg<T>::kKStages;
   constexpr uint32_t kIdesc = ptx::idesc_f16(Cfg<T>::kFmt, 128, 128, 0);
+  constexpr uint32_t kIdescRope = ptx::idesc_f16(Cfg<T>::kRopeFmt, 128, 128, 0);
   const uint32_t kfull0 = ptx::smem_u32(&bars->kfull[0]);
   const uint32_t kempty0 = ptx::smem_u32(&bars->kempty[0]);
   const uint32_t q_full = ptx::smem_u32(&bars->q_full);
@@ -522,7 +711,8 @@ __device__ __forceinline__ void qk_issuer(const Params& p, const Ctx& c, int pai
   Piece pc;
   int piece = 0;
   while (it.next(&pc)) {
-    if (!wait_bar(c, q_full, (uint32_t)piece & 1u, kErrQK)) return;
+    // (FP8: qt_full also covers the Q rows in shared memory, converted)
+    if (!Io<T>::kKv8 && !wait_bar(c, q_full, (uint32_t)piece & 1u, kErrQK)) return;
     if (!wait_bar(c, qt_full, (uint32_t)piece & 1u, kErrQK)) return;
     ptx::tc_fence_after();
 #pragma unroll 1
@@ -551,7 +741,8 @@ __device__ __forceinline__ void qk_issuer(const Params& p, const Ctx& c, int pai
 #pragma unroll
           for (int kk = 0; kk < nk; ++kk)
             ptx::mma_pair_f16(s_tmem, ptx::make_desc(qa + (kk >> 2) * 512 + (kk & 3) * 2, kHiK),
-                              ptx::make_desc(kb + (kk >> 2) * 512 + (kk & 3) * 2, kHiK), kIdesc, 1u);
+                              ptx::make_desc(kb + (kk >> 2) * 512 + (kk & 3) * 2, kHiK),
+                              u < 4 ? kIdesc : kIdescRope, 1u);
         }
         ptx::mma_commit_pair_mc(kempty0 + 8 * ring.stage, 0x3);
         ring.advance();
@@ -646,22 +837,39 @@ __device__ __forceinline__ void pairs_of_sequence(const TileMap& m, int bb, int*
   *pl = m.pair_of(m.first(bb + 1) - 1);
 }
 
+// Two elements of type E, times `scale`, as an fp16 pair (the FP8 variant's Q).
+template <typename E>
+__device__ __forceinline__ uint32_t to_h2_scaled(uint32_t w, float scale) {
+  const float2 f = Elt<E>::to2(w);
+  return Elt<__half>::pack2(f.x * scale, f.y * scale);
+}
+
 // Copy this CTA's staged Q rows, latent dims [0, 256) (four SW128 boxes at
-// `src`: the P buffers for the first piece, else the start of the Q region), into TMEM as the A operand of the first 16 QK^T
-// k-steps: lane L <- row L % 64, so both lane halves hold the rows (the
-// duplicated layout of a pair MMA's A operand in TMEM).
-__device__ __forceinline__ void copy_qt(const uint8_t* src, int m, uint32_t tmem, uint32_t lane_off) {
-#pragma unroll
+// `src`: the P buffers for the first piece, else the start of the Q region), into
+// TMEM as the A operand of the first 16 QK^T k-steps: lane L <- row L % 64, so both
+// lane halves hold the rows (the duplicated layout of a pair MMA's A operand in
+// TMEM).  FP8 variant (K8): converted to fp16 times `scale` on the way.
+template <bool K8, typename E>
+__device__ __forceinline__ void copy_qt(const uint8_t* src, int m, uint32_t tmem, uint32_t lane_off,
+                                        float scale) {
+#pragma unroll 1
   for (int ch = 0; ch < 4; ++ch) {
     const uint8_t* row = src + ch * kChunkBytes + m * 128;
     uint32_t w[32];
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
       const uint4 x = *reinterpret_cast<const uint4*>(row + ((g ^ (m & 7)) << 4));
-      w[4 * g] = x.x;
-      w[4 * g + 1] = x.y;
-      w[4 * g + 2] = x.z;
-      w[4 * g + 3] = x.w;
+      if constexpr (K8) {
+        w[4 * g] = to_h2_scaled<E>(x.x, scale);
+        w[4 * g + 1] = to_h2_scaled<E>(x.y, scale);
+        w[4 * g + 2] = to_h2_scaled<E>(x.z, scale);
+        w[4 * g + 3] = to_h2_scaled<E>(x.w, scale);
+      } else {
+        w[4 * g] = x.x;
+        w[4 * g + 1] = x.y;
+        w[4 * g + 2] = x.z;
+        w[4 * g + 3] = x.w;
+      }
     }
     ptx::tmem_st32(tmem + lane_off + kColQT + 32 * ch, w);
   }
@@ -681,6 +889,9 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
                                                  uint8_t* smem, uint32_t tmem, Barriers* bars, int wq,
                                                  int lane) {
   using S = Smem<T>;
+  using Out = typename Io<T>::Out;   // type of out (and of q)
+  using PT = typename Cfg<T>::PT;    // type of the P operand
+  constexpr bool kK8 = Io<T>::kKv8;
   const int L = wq * 32 + lane;
   const int m = L & 63;
   const int hf = L >> 6;
@@ -730,10 +941,25 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
   // Q dims [0, 256) of piece `k`, staged by the Q loader, into TMEM
   auto take_qt = [&](int k) -> bool {
     if (!wait_bar(c, qts, (uint32_t)k & 1u, kErrSoftmax)) return false;
-    copy_qt(smem + (k == 0 ? S::kP : S::kQ), m, tmem, lane_off);
+    copy_qt<kK8, Out>(smem + (k == 0 ? S::kP : S::kQ), m, tmem, lane_off, p.kv_scale);
     ptx::tc_fence_before();
     __syncwarp();
-    if (lane == 0) {
+    if constexpr (kK8) {
+      // FP8: the Q region is free for this piece's rows once every warp has copied
+      // its staged dims; then its latent dims become scaled fp16 in place
+      if (lane == 0) ptx::mbar_arrive_local(qtr);
+      if (!wait_bar(c, ptx::smem_u32(&bars->qsm), (uint32_t)k & 1u, kErrSoftmax)) return false;
+#pragma unroll 1
+      for (int i = L; i < 4 * 512; i += 128) {
+        uint4* gr = reinterpret_cast<uint4*>(smem + S::kQ + 16 * i);
+        const uint4 x = *gr;
+        *gr = make_uint4(to_h2_scaled<Out>(x.x, p.kv_scale), to_h2_scaled<Out>(x.y, p.kv_scale),
+                         to_h2_scaled<Out>(x.z, p.kv_scale), to_h2_scaled<Out>(x.w, p.kv_scale));
+      }
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive_cluster(qt_full_leader);
+    } else if (lane == 0) {
       ptx::mbar_arrive_local(qtr);
       ptx::mbar_arrive_cluster(qt_full_leader);
     }
@@ -789,8 +1015,8 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         ptx::tmem_wait_ld();
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-          w[k] = pack2<T>(__uint_as_float(a[2 * k]) * scale, __uint_as_float(a[2 * k + 1]) * scale);
-          w[16 + k] = pack2<T>(__uint_as_float(b2[2 * k]) * scale, __uint_as_float(b2[2 * k + 1]) * scale);
+          w[k] = pack2<Out>(__uint_as_float(a[2 * k]) * scale, __uint_as_float(a[2 * k + 1]) * scale);
+          w[16 + k] = pack2<Out>(__uint_as_float(b2[2 * k]) * scale, __uint_as_float(b2[2 * k + 1]) * scale);
         }
         st_box_row(stage + (hf * kHB + i) * kChunkBytes, m, w);
       }
@@ -876,11 +1102,11 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
         const float a = ex2(fmaf(v[2 * k], sl2, -ms));
         const float b2 = ex2(fmaf(v[2 * k + 1], sl2, -ms));
         ls += a + b2;
-        phi[k] = pack2<T>(a, b2);
+        phi[k] = pack2<PT>(a, b2);
         if constexpr (Cfg<T>::kPParts == 2) {
           const float ah = __uint_as_float(phi[k] << 16);
           const float bh = __uint_as_float(phi[k] & 0xffff0000u);
-          plo[k] = pack2<T>(a - ah, b2 - bh);
+          plo[k] = pack2<PT>(a - ah, b2 - bh);
         }
       }
       l += ls;
@@ -935,7 +1161,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
       *merge_flag = (ptx::ld_acquire_gpu(cnt) + 1u == npieces) ? 1u : 0u;
     if (!sync4(lx, n_lx)) return;
     const float ltot = l + xl[L ^ 64];
-    const float inv = 1.f / ltot;
+    const float inv = (kK8 ? p.kv_scale : 1.f) / ltot;   // FP8: V's scale, folded here
     const float lse = (m_run * sl2 + log2f(ltot)) * kLn2;
     const int head = 64 * (int)rank + m;                   // row within the head group
     const int hglob = vseq_head0(p, pc.bb) + head;         // head within the sequence
@@ -1080,11 +1306,12 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
             for (int g = 0; g < 8; ++g)
               dst[g] = make_float4(acc[4 * g], acc[4 * g + 1], acc[4 * g + 2], acc[4 * g + 3]);
           } else {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + orow + d0);
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<Out*>(p.out) + orow + d0);
 #pragma unroll
             for (int g = 0; g < 4; ++g)
-              dst[g] = make_uint4(pack2<T>(acc[8 * g], acc[8 * g + 1]), pack2<T>(acc[8 * g + 2], acc[8 * g + 3]),
-                                  pack2<T>(acc[8 * g + 4], acc[8 * g + 5]), pack2<T>(acc[8 * g + 6], acc[8 * g + 7]));
+              dst[g] = make_uint4(pack2<Out>(acc[8 * g], acc[8 * g + 1]), pack2<Out>(acc[8 * g + 2], acc[8 * g + 3]),
+                                  pack2<Out>(acc[8 * g + 4], acc[8 * g + 5]),
+                                  pack2<Out>(acc[8 * g + 6], acc[8 * g + 7]));
           }
         }
       }
@@ -1106,7 +1333,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
 // (warps 9..11 complete the third warpgroup)
 // ---------------------------------------------------------------------------
 template <typename T>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_of<T>(), 1)
 mla_sm100_decode_kernel(const __grid_constant__ Params p) {
   using S = Smem<T>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1121,12 +1348,21 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
   const int pair = blockIdx.x >> 1;
 
   if (threadIdx.x == 0) {
+    // operand stages: one expect-tx arrival (TMA), or FP8: 2 converter warps x 2 CTAs
+    const uint32_t n_full = Io<T>::kKv8 ? 4u : 1u;
     for (int s = 0; s < 8; ++s) {
-      ptx::mbar_init(ptx::smem_u32(&bars->kfull[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&bars->kfull[s]), n_full);
       ptx::mbar_init(ptx::smem_u32(&bars->kempty[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&bars->vfull[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&bars->vfull[s]), n_full);
       ptx::mbar_init(ptx::smem_u32(&bars->vempty[s]), 1);
     }
+    for (int s = 0; s < 4; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&bars->k8full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&bars->k8empty[s]), 2);
+      ptx::mbar_init(ptx::smem_u32(&bars->v8full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&bars->v8empty[s]), 2);
+    }
+    ptx::mbar_init(ptx::smem_u32(&bars->qsm), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->q_full), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->q_empty), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->qt_full), 8);
@@ -1199,6 +1435,9 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
       ptx::mma_commit_pair_mc(ptx::smem_u32(&bars->drain_pv), 0x1);
       wait_bar(c, ptx::smem_u32(&bars->drain_pv), 0u, kErrDrain);
     }
+  } else if (Io<T>::kKv8 && warp >= 12) {
+    // FP8: warps 12, 13 convert the K stages, warps 14, 15 the V stages
+    converter<T>(p, c, pair, smem, bars, warp < 14, (warp & 1) * 32 + lane, lane);
   }
   }
   __syncwarp();
@@ -1384,12 +1623,12 @@ bool make_map3(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, u
 // KV rows [rows][kv_heads][cols] (row-major), boxes of 64 rows x 1 KV head x 128
 // bytes, 128-byte swizzle: the smem tile of one KV head is the 2D 64 x 128-byte box.
 bool make_map_kv(CUtensorMap* m, const void* base, uint64_t cols, uint64_t kv_heads, uint64_t rows,
-                 CUtensorMapDataType dt) {
+                 CUtensorMapDataType dt, uint32_t elem_bytes = 2) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[3] = {cols, kv_heads, rows};
-  const cuuint64_t strides[2] = {cols * 2, kv_heads * cols * 2};
-  const cuuint32_t box[3] = {64, 1, 64};
+  const cuuint64_t strides[2] = {cols * elem_bytes, kv_heads * cols * elem_bytes};
+  const cuuint32_t box[3] = {128 / elem_bytes, 1, 64};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1411,7 +1650,7 @@ cudaError_t set_attrs_and_count(int* pairs) {
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * 74, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(threads_of<T>(), 1, 1);
   cfg.dynamicSmemBytes = Smem<T>::kBytes;
   cudaLaunchAttribute attr{};
   attr.id = cudaLaunchAttributeClusterDimension;
@@ -1427,12 +1666,14 @@ cudaError_t device_info(int dev, DeviceInfo* out) {
   std::lock_guard<std::mutex> lock(g_dev_mutex);
   DeviceInfo& d = g_dev[dev];
   if (!d.ready) {
-    int nb = 0, nh = 0;
-    cudaError_t err = set_attrs_and_count<__nv_bfloat16>(&nb);
+    int n[4] = {0, 0, 0, 0};
+    cudaError_t err = set_attrs_and_count<__nv_bfloat16>(&n[0]);
+    if (err == cudaSuccess) err = set_attrs_and_count<__half>(&n[1]);
+    if (err == cudaSuccess) err = set_attrs_and_count<Kv8<__nv_bfloat16>>(&n[2]);
+    if (err == cudaSuccess) err = set_attrs_and_count<Kv8<__half>>(&n[3]);
     if (err != cudaSuccess) return err;
-    err = set_attrs_and_count<__half>(&nh);
-    if (err != cudaSuccess) return err;
-    d.max_pairs = nb < nh ? nb : nh;
+    d.max_pairs = n[0];
+    for (int i = 1; i < 4; ++i) d.max_pairs = n[i] < d.max_pairs ? n[i] : d.max_pairs;
     d.ready = true;
   }
   *out = d;
@@ -1542,8 +1783,10 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
   const uint64_t kv_rows = a.block_table != nullptr ? (uint64_t)a.num_pages * a.page_size
                                                     : (uint64_t)a.batch * a.seqlen_kv;
   const QShape qs = qshape(a);
-  if (!make_map_kv(&p.tm_kv, a.kv, kDim, qs.kv_heads, kv_rows, dt) ||
-      !make_map_kv(&p.tm_kpe, a.k_pe, kPeDim, qs.kv_heads, kv_rows, dt) ||
+  const bool ok_kv = a.kv_fp8 ? make_map_kv(&p.tm_kv, a.kv, kDim, qs.kv_heads, kv_rows,
+                                            CU_TENSOR_MAP_DATA_TYPE_UINT8, 1)
+                               : make_map_kv(&p.tm_kv, a.kv, kDim, qs.kv_heads, kv_rows, dt);
+  if (!ok_kv || !make_map_kv(&p.tm_kpe, a.k_pe, kPeDim, qs.kv_heads, kv_rows, dt) ||
       !make_map3(&p.tm_q, a.q, kDim, qs.g, qs.qb, dt) || !make_map3(&p.tm_qpe, a.q_pe, kPeDim, qs.g, qs.qb, dt))
     return cudaErrorInvalidValue;
   p.out_f32 = a.out_dtype == MLA_DTYPE_F32 ? 1 : 0;
@@ -1579,11 +1822,21 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
   p.block_table = a.block_table;
   p.page_size = a.page_size;
   p.max_pages = a.max_pages;
-  if (a.dtype == MLA_DTYPE_BF16)
+  p.kv_scale = a.kv_fp8 ? a.kv_scale : 1.f;
+  if (a.kv_fp8) {
+    if (a.dtype == MLA_DTYPE_BF16)
+      mla_sm100_decode_kernel<Kv8<__nv_bfloat16>><<<2 * pairs, threads_of<Kv8<__nv_bfloat16>>(),
+                                                    Smem<Kv8<__nv_bfloat16>>::kBytes, a.stream>>>(p);
+    else
+      mla_sm100_decode_kernel<Kv8<__half>>
+          <<<2 * pairs, threads_of<Kv8<__half>>(), Smem<Kv8<__half>>::kBytes, a.stream>>>(p);
+  } else if (a.dtype == MLA_DTYPE_BF16) {
     mla_sm100_decode_kernel<__nv_bfloat16>
-        <<<2 * pairs, kThreads, Smem<__nv_bfloat16>::kBytes, a.stream>>>(p);
-  else
-    mla_sm100_decode_kernel<__half><<<2 * pairs, kThreads, Smem<__half>::kBytes, a.stream>>>(p);
+        <<<2 * pairs, threads_of<__nv_bfloat16>(), Smem<__nv_bfloat16>::kBytes, a.stream>>>(p);
+  } else {
+    mla_sm100_decode_kernel<__half>
+        <<<2 * pairs, threads_of<__half>(), Smem<__half>::kBytes, a.stream>>>(p);
+  }
   return cudaGetLastError();
 }
 

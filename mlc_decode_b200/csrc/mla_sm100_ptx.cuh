@@ -106,6 +106,15 @@ __device__ __forceinline__ void tma_load_3d_pair_hint(uint32_t dst_smem, const v
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d_local_hint(uint32_t dst_smem, const void* desc, uint32_t bar,
+                                                       int32_t x, int32_t y, int32_t z, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(dst_smem),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar), "r"(x), "r"(y), "r"(z), "l"(policy)
+      : "memory");
+}
+
 // L2 eviction-priority policies for cache-hinted loads: keep lines that are
 // read again soon, let lines read for the last time go first.
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {

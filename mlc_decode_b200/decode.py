@@ -20,6 +20,7 @@ from . import capi
 DIM = 512
 PE_DIM = 64
 _DTYPES = {torch.float16: capi.MLA_DTYPE_F16, torch.bfloat16: capi.MLA_DTYPE_BF16}
+_FP8 = getattr(torch, "float8_e4m3fn", torch.uint8)
 
 
 def _check_tensor(name, t, shape, dtype, device):
@@ -43,7 +44,7 @@ class MlaDecodeKernel:
     ``cfg`` is a reference-style config dict (keys block_N, block_H, num_split,
     spread, num_stages, combine_groups; plus ``kernel`` = "auto"/"simt"/"tc"),
     or None to let the library choose.  dim == 512 and pe_dim == 64.  The
-    reference's kernels take kv_heads == 1 only (mla_decode.py:16); here
+    reference's kernels take kv_heads == 1 only (baseline_mla.py:16); here
     kv_head_num > 1 (heads a multiple of it, kv [batch, kv_ctx, kv_head_num,
     512]) runs through mla_decode_ext with the reference ref_program's head
     grouping, for ``__call__`` only.
@@ -126,6 +127,37 @@ class MlaDecodeKernel:
             stream = torch.cuda.current_stream(dev).cuda_stream
         capi.decode_fwd(q.data_ptr(), q_pe.data_ptr(), kv.data_ptr(), k_pe.data_ptr(), out.data_ptr(),
                         lse_ptr, ws.data_ptr(), ws.numel(), b, h, s, _DTYPES[dtype], self._ccfg, stream)
+
+    def decode_fp8(self, q, q_pe, kv_fp8, k_pe, kv_scale, out, lse=None):
+        """``__call__`` over an FP8 latent cache (mla_decode_fp8kv).
+
+        ``kv_fp8`` [batch, kv_ctx, 1, 512] holds e4m3 values (``torch.float8_e4m3fn``,
+        or their bytes as ``torch.uint8``); the latent rows are ``kv_fp8 * kv_scale``.
+        q, q_pe, k_pe and out keep the model dtype.  Tensor-core kernel only.
+        """
+        self._one_kv_head("decode_fp8")
+        b, h, s = self.batch, self.heads, self.seqlen_kv
+        dtype = q.dtype if isinstance(q, torch.Tensor) else None
+        if dtype not in _DTYPES:
+            raise ValueError(f"q must be float16 or bfloat16, got {dtype}")
+        if not isinstance(kv_fp8, torch.Tensor) or kv_fp8.dtype not in (torch.uint8, _FP8):
+            raise ValueError("kv_fp8 must be a torch.float8_e4m3fn (or uint8) tensor")
+        dev = q.device
+        _check_tensor("q", q, (b, h, DIM), dtype, None)
+        _check_tensor("q_pe", q_pe, (b, h, PE_DIM), dtype, dev)
+        _check_tensor("kv_fp8", kv_fp8, (b, s, 1, DIM), kv_fp8.dtype, dev)
+        _check_tensor("k_pe", k_pe, (b, s, 1, PE_DIM), dtype, dev)
+        _check_tensor("out", out, (b, h, DIM), dtype, dev)
+        lse_ptr = None
+        if lse is not None:
+            _check_tensor("lse", lse, (b, h), torch.float32, dev)
+            lse_ptr = lse.data_ptr()
+        ws = self._workspace(dev, dtype)
+        with torch.cuda.device(dev):
+            stream = torch.cuda.current_stream(dev).cuda_stream
+        capi.decode_fp8kv(q.data_ptr(), q_pe.data_ptr(), kv_fp8.data_ptr(), k_pe.data_ptr(), float(kv_scale),
+                          out.data_ptr(), lse_ptr, ws.data_ptr(), ws.numel(), b, h, s, _DTYPES[dtype], self._ccfg,
+                          stream)
 
     def partial(self, q, q_pe, kv, k_pe, o, lse):
         """Decode against this KV part with a float32 result (mla_decode_partial).

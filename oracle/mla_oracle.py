@@ -19,6 +19,10 @@ It restates, on the CPU, the algorithm of the reference project
 * ``splitkv_partials_f64`` / ``combine_f64`` -- the split-KV main kernel's
   per-split partial output and LSE (``mla_decode.py:113-192``) and the LSE
   combine (``mla_decode.py:194-246``), in float64 and natural-log units.
+* ``ref_grouped_f64`` / ``ref_multi_token_f64`` -- ``ref_program`` with kv_heads > 1
+  and per query position of a multi-token step; ``quantize_e4m3`` /
+  ``ref_fp8kv_f64`` -- the FP8 latent cache format and ``ref_program`` over the
+  dequantized cache (paths the reference does not have).
 
 Parity is pinned by ``tests/golden/`` fixtures produced by importing the
 reference's own ``baseline_mla.ref_program`` and ``mla_decode._split_plan``
@@ -179,6 +183,26 @@ def ref_multi_token_f64(q, q_pe, kv, k_pe, lens=None):
             o, l = ref_grouped_f64(q[bb:bb + 1, t], q_pe[bb:bb + 1, t], kv[bb:bb + 1, :n], k_pe[bb:bb + 1, :n])
             out[bb, t], lse[bb, t] = o[0], l[0]
     return out, lse
+
+
+def quantize_e4m3(kv, scale):
+    """e4m3 (torch.float8_e4m3fn) codes of kv / scale, round to nearest, saturating
+    at +-448 (the FP8 latent cache format of mla_decode_fp8kv)."""
+    import torch
+
+    x = (kv.float() / float(scale)).clamp(-448.0, 448.0)
+    return x.to(torch.float8_e4m3fn)
+
+
+def ref_fp8kv_f64(q, q_pe, kv_fp8, k_pe, scale):
+    """The reference's ``ref_program`` (baseline_mla.py:177-191) over the
+    dequantized FP8 cache kv_fp8 * scale, exactly (e4m3 -> float64 is exact).
+    The reference has no FP8 path (its notes list FP8 KV as untried,
+    docs/mla_decode_best_implementation.md:1693); this is the oracle for one."""
+    import torch
+
+    kv = kv_fp8.to(torch.float64) * float(scale)
+    return ref_program_f64(q, q_pe, kv, k_pe)
 
 
 def split_plan(seqlen_kv, num_split, block_n, spread=False):
