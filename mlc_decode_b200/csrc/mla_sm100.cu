@@ -94,8 +94,8 @@ struct Cfg<__nv_bfloat16> {
   static constexpr uint32_t kRopeFmt = 1;
   static constexpr int kPParts = 2;
   static constexpr int kKStages = 4;
+  static constexpr uint32_t kKStageBytes = kStageBytes;
   static constexpr int kVStages = 3;
-  static constexpr int kK8Stages = 0;
   static constexpr int kV8Stages = 0;
   using PT = __nv_bfloat16;   // P operand type
 };
@@ -105,17 +105,22 @@ struct Cfg<__half> {
   static constexpr uint32_t kRopeFmt = 0;
   static constexpr int kPParts = 1;
   static constexpr int kKStages = 6;
+  static constexpr uint32_t kKStageBytes = kStageBytes;
   static constexpr int kVStages = 3;
-  static constexpr int kK8Stages = 0;
   static constexpr int kV8Stages = 0;
   using PT = __half;
 };
 
-// The FP8 variant: latent KV rows in e4m3 (one byte per dim), dequantized to fp16
-// in shared memory by converter warps; every latent MMA and P run in fp16 (e4m3 ->
-// fp16 is exact; fp16 P needs no hi/lo pair).  T is the type of q, q_pe, k_pe
-// and out; the rope MMAs stay in T.  The tensor's scale is folded into Q's latent
-// dims (once per piece) and into the output normalisation.
+// The FP8 variant: latent KV rows in e4m3 (one byte per dim).  QK^T runs on the
+// e4m3 tiles as loaded (kind::f8f6f4) against Q split into two e4m3 parts,
+// hi = e4m3(q a) and lo = e4m3(q a - hi), a a per-row power of two that puts the
+// row's largest |q a| near 224 (hi from TMEM, lo from shared memory): 8
+// significant bits, exact for bf16 q.  The rope dims run in T against
+// q_pe a / s as a T hi/lo pair (s the cache's scale), so the scores come out as
+// (a / s) x the true ones and the softmax multiplies by s / a.  V is dequantized
+// to fp16 in shared memory by converter warps (exact) and P.V runs in fp16 with
+// fp16 P (no hi/lo pair); s is folded into the output normalisation.  T is the
+// type of q, q_pe, k_pe and out.
 template <typename T>
 struct Kv8 {};
 template <typename K>
@@ -133,10 +138,10 @@ struct Cfg<Kv8<T>> {
   static constexpr uint32_t kFmt = 0;
   static constexpr uint32_t kRopeFmt = Cfg<T>::kFmt;
   static constexpr int kPParts = 1;
-  static constexpr int kKStages = 3;    // fp16 operand stages (16 KB)
-  static constexpr int kVStages = 2;
-  static constexpr int kK8Stages = 4;   // e4m3 (or rope) stages as loaded (8 KB)
-  static constexpr int kV8Stages = 4;
+  static constexpr int kKStages = 8;                 // e4m3 latent or rope units as loaded
+  static constexpr uint32_t kKStageBytes = kChunkBytes;
+  static constexpr int kVStages = 3;                 // fp16 V operand stages (16 KB)
+  static constexpr int kV8Stages = 3;                // e4m3 V units as loaded (8 KB)
   using PT = __half;
 };
 template <typename K>
@@ -145,9 +150,7 @@ constexpr int threads_of() { return Io<K>::kKv8 ? 512 : 384; }
 struct Barriers {
   uint64_t kfull[8], kempty[8];
   uint64_t vfull[8], vempty[8];
-  uint64_t k8full[4], k8empty[4];   // FP8 variant: e4m3 stages as loaded
-  uint64_t v8full[4], v8empty[4];
-  uint64_t qsm;                     // FP8 variant: this CTA's Q rows in shared memory
+  uint64_t v8full[4], v8empty[4];   // FP8 variant: e4m3 V units as loaded
   uint64_t q_full, q_empty, qt_full;
   uint64_t s_full[2], s_free[2];
   uint64_t p_full[2];
@@ -163,12 +166,13 @@ static_assert(sizeof(Barriers) <= 1024, "barrier block");
 template <typename T>
 struct Smem {
   static constexpr uint32_t kQ = 0;
-  static constexpr uint32_t kP = kQ + kQBytes;
+  // Q region: 4 latent boxes (fp16/bf16 dims [256, 512), or the FP8 variant's e4m3 lo
+  // of all 512 dims) and the rope box (FP8: the rope hi and lo boxes)
+  static constexpr uint32_t kP = kQ + (Io<T>::kKv8 ? 6 * kChunkBytes : kQBytes);
   static constexpr uint32_t kPBuf = Cfg<T>::kPParts * kPBytes;     // one P buffer (hi [, lo])
   static constexpr uint32_t kKRing = kP + 2 * kPBuf;
-  static constexpr uint32_t kVRing = kKRing + Cfg<T>::kKStages * kStageBytes;
-  static constexpr uint32_t kK8Ring = kVRing + Cfg<T>::kVStages * kStageBytes;
-  static constexpr uint32_t kV8Ring = kK8Ring + Cfg<T>::kK8Stages * kChunkBytes;
+  static constexpr uint32_t kVRing = kKRing + Cfg<T>::kKStages * Cfg<T>::kKStageBytes;
+  static constexpr uint32_t kV8Ring = kVRing + Cfg<T>::kVStages * kStageBytes;
   static constexpr uint32_t kBar = kV8Ring + Cfg<T>::kV8Stages * kChunkBytes;
   static constexpr uint32_t kXmax = kBar + 1024;
   static constexpr uint32_t kXl = kXmax + 2 * 128 * 4;
@@ -416,12 +420,8 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
   const uint64_t once = ptx::l2_policy_evict_first();
   Piece pc;
   if constexpr (Io<T>::kKv8) {
-    // FP8: this CTA's e4m3 latent units (64 rows x 128 dims, 8 KB) and its rope
-    // unit into the e4m3 ring, each on a local barrier; the converter warps turn
-    // them into the fp16 operand ring
-    const uint32_t k8full0 = ptx::smem_u32(&bars->k8full[0]);
-    const uint32_t k8empty0 = ptx::smem_u32(&bars->k8empty[0]);
-    Ring<Cfg<T>::kK8Stages> r8;
+    // FP8: per tile 4 e4m3 latent units (64 rows x 128 dims, one 8 KB box) and the
+    // rope unit, straight into the K ring for the kind::f8f6f4 QK^T
     while (it.next(&pc)) {
       const int kseq = vseq_kvseq(p, pc.bb), kvh = vseq_kvh(p, pc.bb), klen = seq_len(p, pc.bb);
 #pragma unroll 1
@@ -429,15 +429,15 @@ __device__ __forceinline__ void k_producer(const Params& p, const Ctx& c, uint32
         const int y = kv_row(p, kseq, j * kTile + 64 * (int)rank, klen);
 #pragma unroll 1
         for (int u = 0; u < 5; ++u) {
-          if (!wait_bar(c, k8empty0 + 8 * r8.stage, r8.phase ^ 1u, kErrKLoad)) return;
-          const uint32_t bar = k8full0 + 8 * r8.stage;
-          const uint32_t dst = sbase + S::kK8Ring + r8.stage * kChunkBytes;
-          ptx::mbar_arrive_expect_tx(bar, kChunkBytes);
+          if (!wait_bar(c, kempty0 + 8 * ring.stage, ring.phase ^ 1u, kErrKLoad)) return;
+          if (leader) ptx::mbar_arrive_expect_tx(kfull0 + 8 * ring.stage, 2 * kChunkBytes);
+          const uint32_t dst = sbase + S::kKRing + ring.stage * kChunkBytes;
+          const uint32_t bar = kfull0_leader + 8 * ring.stage;
           if (u < 4)
-            ptx::tma_load_3d_local_hint(dst, &p.tm_kv, bar, 128 * u, kvh, y, keep);
+            ptx::tma_load_3d_pair_hint(dst, &p.tm_kv, bar, 128 * u, kvh, y, keep);
           else
-            ptx::tma_load_3d_local_hint(dst, &p.tm_kpe, bar, 0, kvh, y, once);
-          r8.advance();
+            ptx::tma_load_3d_pair_hint(dst, &p.tm_kpe, bar, 0, kvh, y, once);
+          ring.advance();
         }
       }
     }
@@ -497,6 +497,18 @@ __device__ __forceinline__ void q_loader(const Params& p, const Ctx& c, uint32_t
   const uint32_t qtr = ptx::smem_u32(&bars->qtr);
   const uint32_t q_go = ptx::smem_u32(&bars->q_go);
   PieceIter it(p, pair);
+  if constexpr (Io<T>::kKv8) {
+    // FP8: the softmax warps read each piece's Q rows from global memory (they
+    // quantize them); this thread only pulls the rows into L2 ahead of time
+    Piece pq;
+    bool first = true;
+    while (it.next(&pq)) {
+      prefetch_q(p, pq.bb, rank);
+      if (first) ptx::mbar_arrive_local(q_go);
+      first = false;
+    }
+    return;
+  }
   {
     PieceIter first = it;
     Piece p0;
@@ -519,23 +531,12 @@ __device__ __forceinline__ void q_loader(const Params& p, const Ctx& c, uint32_t
     for (int ch = 0; ch < 4; ++ch)
       ptx::tma_load_3d_local(qt_dst + ch * kChunkBytes, &p.tm_q, qts, 64 * ch, qrow, qseq);
     if (piece > 0 && !wait_bar(c, qtr, (uint32_t)piece & 1u, kErrKLoad)) return;
-    if constexpr (Io<T>::kKv8) {
-      // FP8: local loads; the softmax warps convert the latent dims to scaled fp16
-      // in place before they release the piece's Q to the QK^T issuer
-      const uint32_t qsm = ptx::smem_u32(&bars->qsm);
-      ptx::mbar_arrive_expect_tx(qsm, kQBytes);
+    if (leader) ptx::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
 #pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch)
-        ptx::tma_load_3d_local(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, qsm, kQTDims + 64 * ch, qrow, qseq);
-      ptx::tma_load_3d_local(sbase + S::kQ + 4 * kChunkBytes, &p.tm_qpe, qsm, 0, qrow, qseq);
-    } else {
-      if (leader) ptx::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
-#pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch)
-        ptx::tma_load_3d_pair(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, q_full_leader, kQTDims + 64 * ch,
-                              qrow, qseq);
-      ptx::tma_load_3d_pair(sbase + S::kQ + 4 * kChunkBytes, &p.tm_qpe, q_full_leader, 0, qrow, qseq);
-    }
+    for (int ch = 0; ch < 4; ++ch)
+      ptx::tma_load_3d_pair(sbase + S::kQ + ch * kChunkBytes, &p.tm_q, q_full_leader, kQTDims + 64 * ch,
+                            qrow, qseq);
+    ptx::tma_load_3d_pair(sbase + S::kQ + 4 * kChunkBytes, &p.tm_qpe, q_full_leader, 0, qrow, qseq);
     if (piece == 0) ptx::mbar_arrive_local(q_go);
     ++piece;
   }
@@ -609,78 +610,73 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
 }
 
 // ---------------------------------------------------------------------------
-// FP8 variant: converter warps.  Two warps per side (K: latent units + the rope
-// unit of each tile; V: the four units of each tile) take an e4m3 stage (64 rows x
-// 128 dims, one SW128 box) and write the fp16 operand stage the MMAs read (the same
-// rows as two SW128 boxes of 64 dims), then release the e4m3 stage (local) and
-// signal the operand stage to the even CTA's issuer (count 2 warps x 2 CTAs).
-// e4m3 -> fp16 is exact.  The rope unit is copied as loaded (already in the
-// operand layout).
+// FP8 variant: V converter warps (warps 12..15).  All four take every e4m3 V unit
+// (64 tokens x 128 dims, one SW128 box), each a quarter of its 16-byte granules,
+// and write the fp16 operand stage P.V reads (the same rows as two SW128 boxes of
+// 64 dims); then each releases the e4m3 stage (local, count 4) and signals the
+// operand stage to the even CTA's P.V issuer (count 4 warps x 2 CTAs).  e4m3 ->
+// fp16 is exact.
 // ---------------------------------------------------------------------------
+constexpr int kConvWarps = 4;
+
 __device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t v) {
   const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(v & 0xffffu), __NV_E4M3);
   return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
 
 template <typename T>
-__device__ __forceinline__ void converter(const Params& p, const Ctx& c, int pair, uint8_t* smem,
-                                          Barriers* bars, bool kside, int ct, int lane) {
+__device__ __forceinline__ void v_converter(const Params& p, const Ctx& c, int pair, uint8_t* smem,
+                                            Barriers* bars, int ct, int lane) {
   using S = Smem<T>;
-  const uint32_t full8 = ptx::smem_u32(kside ? &bars->k8full[0] : &bars->v8full[0]);
-  const uint32_t empty8 = ptx::smem_u32(kside ? &bars->k8empty[0] : &bars->v8empty[0]);
-  const uint32_t op_empty = ptx::smem_u32(kside ? &bars->kempty[0] : &bars->vempty[0]);
-  const uint32_t op_full_leader = ptx::mapa(ptx::smem_u32(kside ? &bars->kfull[0] : &bars->vfull[0]), 0);
-  const uint8_t* ring8 = smem + (kside ? S::kK8Ring : S::kV8Ring);
-  uint8_t* ring_op = smem + (kside ? S::kKRing : S::kVRing);
-  const uint32_t n8 = kside ? Cfg<T>::kK8Stages : Cfg<T>::kV8Stages;
-  const uint32_t n_op = kside ? Cfg<T>::kKStages : Cfg<T>::kVStages;
-  const int units = kside ? 5 : 4;
-  const uint32_t code = kside ? kErrKLoad : kErrVLoad;
-  uint32_t s8 = 0, ph8 = 0, so = 0, pho = 0;
+  constexpr int kPer = 512 / (32 * kConvWarps);   // granules per thread and unit
+  const uint32_t full8 = ptx::smem_u32(&bars->v8full[0]);
+  const uint32_t empty8 = ptx::smem_u32(&bars->v8empty[0]);
+  const uint32_t op_empty = ptx::smem_u32(&bars->vempty[0]);
+  const uint32_t op_full_leader = ptx::mapa(ptx::smem_u32(&bars->vfull[0]), 0);
+  const uint8_t* ring8 = smem + S::kV8Ring;
+  uint8_t* ring_op = smem + S::kVRing;
+  Ring<Cfg<T>::kV8Stages> r8;
+  Ring<Cfg<T>::kVStages> rop;
   PieceIter it(p, pair);
   Piece pc;
   while (it.next(&pc)) {
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j) {
 #pragma unroll 1
-      for (int u = 0; u < units; ++u) {
-        if (!wait_bar(c, full8 + 8 * s8, ph8, code)) return;
-        if (!wait_bar(c, op_empty + 8 * so, pho ^ 1u, code)) return;
-        const uint8_t* src = ring8 + s8 * kChunkBytes;
-        uint8_t* dst = ring_op + so * kStageBytes;
-        if (kside && u == 4) {
+      for (int u = 0; u < 4; ++u) {
+        if (!wait_bar(c, full8 + 8 * r8.stage, r8.phase, kErrVLoad)) return;
+        if (!wait_bar(c, op_empty + 8 * rop.stage, rop.phase ^ 1u, kErrVLoad)) return;
+        const uint8_t* src = ring8 + r8.stage * kChunkBytes;
+        uint8_t* dst = ring_op + rop.stage * kStageBytes;
+        // all of this thread's granules in flight before any conversion
+        uint4 x[kPer];
 #pragma unroll
-          for (int i = ct; i < 512; i += 64)
-            *reinterpret_cast<uint4*>(dst + 16 * i) = *reinterpret_cast<const uint4*>(src + 16 * i);
-        } else {
-#pragma unroll 4
-          for (int i = ct; i < 512; i += 64) {
-            // logical 16-byte granule g of row r (elements [16 g, 16 g + 16)) sits at g ^ (r & 7)
-            const int r = i >> 3, g = i & 7;
-            const uint4 x = *reinterpret_cast<const uint4*>(src + r * 128 + ((g ^ (r & 7)) << 4));
-            uint8_t* row = dst + (g >> 2) * kChunkBytes + r * 128;
-            const int g1 = 2 * (g & 3);
-            *reinterpret_cast<uint4*>(row + ((g1 ^ (r & 7)) << 4)) =
-                make_uint4(e4m3x2_to_h2(x.x), e4m3x2_to_h2(x.x >> 16), e4m3x2_to_h2(x.y), e4m3x2_to_h2(x.y >> 16));
-            *reinterpret_cast<uint4*>(row + (((g1 + 1) ^ (r & 7)) << 4)) =
-                make_uint4(e4m3x2_to_h2(x.z), e4m3x2_to_h2(x.z >> 16), e4m3x2_to_h2(x.w), e4m3x2_to_h2(x.w >> 16));
-          }
+        for (int k = 0; k < kPer; ++k) {
+          // logical 16-byte granule g of row r (elements [16 g, 16 g + 16)) sits at g ^ (r & 7)
+          const int i = ct + 32 * kConvWarps * k, r = i >> 3, g = i & 7;
+          x[k] = *reinterpret_cast<const uint4*>(src + r * 128 + ((g ^ (r & 7)) << 4));
+        }
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+          const int i = ct + 32 * kConvWarps * k, r = i >> 3, g = i & 7;
+          uint8_t* row = dst + (g >> 2) * kChunkBytes + r * 128;
+          const int g1 = 2 * (g & 3);
+          *reinterpret_cast<uint4*>(row + ((g1 ^ (r & 7)) << 4)) =
+              make_uint4(e4m3x2_to_h2(x[k].x), e4m3x2_to_h2(x[k].x >> 16), e4m3x2_to_h2(x[k].y),
+                         e4m3x2_to_h2(x[k].y >> 16));
+          *reinterpret_cast<uint4*>(row + (((g1 + 1) ^ (r & 7)) << 4)) =
+              make_uint4(e4m3x2_to_h2(x[k].z), e4m3x2_to_h2(x[k].z >> 16), e4m3x2_to_h2(x[k].w),
+                         e4m3x2_to_h2(x[k].w >> 16));
         }
         // the tensor core reads the stage through the async proxy
         ptx::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          ptx::mbar_arrive_local(empty8 + 8 * s8);
-          ptx::mbar_arrive_cluster(op_full_leader + 8 * so);
+          ptx::mbar_arrive_local(empty8 + 8 * r8.stage);
+          ptx::mbar_arrive_cluster(op_full_leader + 8 * rop.stage);
         }
-        if (++s8 == n8) {
-          s8 = 0;
-          ph8 ^= 1u;
-        }
-        if (++so == n_op) {
-          so = 0;
-          pho ^= 1u;
-        }
+        r8.advance();
+        rop.advance();
       }
     }
   }
@@ -711,7 +707,7 @@ __device__ __forceinline__ void qk_issuer(const Params& p, const Ctx& c, int pai
   Piece pc;
   int piece = 0;
   while (it.next(&pc)) {
-    // (FP8: qt_full also covers the Q rows in shared memory, converted)
+    // (FP8: qt_full covers the whole quantized Q, written by the softmax warps)
     if (!Io<T>::kKv8 && !wait_bar(c, q_full, (uint32_t)piece & 1u, kErrQK)) return;
     if (!wait_bar(c, qt_full, (uint32_t)piece & 1u, kErrQK)) return;
     ptx::tc_fence_after();
@@ -727,8 +723,18 @@ __device__ __forceinline__ void qk_issuer(const Params& p, const Ctx& c, int pai
         if (!wait_bar(c, kfull0 + 8 * ring.stage, ring.phase, kErrQK)) return;
         ptx::tc_fence_after();
         // descriptor low words; +512 = next 8 KB box, +2 = next 32-byte k-step
-        const uint32_t kb = ptx::sw128_desc_lo(sbase + S::kKRing + ring.stage * kStageBytes, 16);
-        if (u < 2) {
+        const uint32_t kb = ptx::sw128_desc_lo(sbase + S::kKRing + ring.stage * Cfg<T>::kKStageBytes, 16);
+        if (Io<T>::kKv8 && u < 4) {
+          // FP8: latent dims [128 u, +128) in e4m3, 32 per k-step: Q hi from TMEM (4
+          // elements per column), Q lo from box u of the Q region
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t bd = ptx::make_desc(kb + kk * 2, kHiK);
+            ptx::mma_pair_f8_ts(s_tmem, tmem + kColQT + 8 * (4 * u + kk), bd, kIdesc,
+                                (u == 0 && kk == 0) ? 0u : 1u);
+            ptx::mma_pair_f8(s_tmem, ptx::make_desc(qlo + u * 512 + kk * 2, kHiK), bd, kIdesc, 1u);
+          }
+        } else if (!Io<T>::kKv8 && u < 2) {
           // latent dims [0, 256): Q from TMEM, 8 columns (16 elements) per k-step
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
@@ -743,6 +749,13 @@ __device__ __forceinline__ void qk_issuer(const Params& p, const Ctx& c, int pai
             ptx::mma_pair_f16(s_tmem, ptx::make_desc(qa + (kk >> 2) * 512 + (kk & 3) * 2, kHiK),
                               ptx::make_desc(kb + (kk >> 2) * 512 + (kk & 3) * 2, kHiK),
                               u < 4 ? kIdesc : kIdescRope, 1u);
+          if (Io<T>::kKv8) {
+            // FP8: the rope's lo part (box 5 of the Q region)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              ptx::mma_pair_f16(s_tmem, ptx::make_desc(qlo + 5 * 512 + kk * 2, kHiK), ptx::make_desc(kb + kk * 2, kHiK),
+                                kIdescRope, 1u);
+          }
         }
         ptx::mma_commit_pair_mc(kempty0 + 8 * ring.stage, 0x3);
         ring.advance();
@@ -837,39 +850,23 @@ __device__ __forceinline__ void pairs_of_sequence(const TileMap& m, int bb, int*
   *pl = m.pair_of(m.first(bb + 1) - 1);
 }
 
-// Two elements of type E, times `scale`, as an fp16 pair (the FP8 variant's Q).
-template <typename E>
-__device__ __forceinline__ uint32_t to_h2_scaled(uint32_t w, float scale) {
-  const float2 f = Elt<E>::to2(w);
-  return Elt<__half>::pack2(f.x * scale, f.y * scale);
-}
-
 // Copy this CTA's staged Q rows, latent dims [0, 256) (four SW128 boxes at
 // `src`: the P buffers for the first piece, else the start of the Q region), into
 // TMEM as the A operand of the first 16 QK^T k-steps: lane L <- row L % 64, so both
 // lane halves hold the rows (the duplicated layout of a pair MMA's A operand in
-// TMEM).  FP8 variant (K8): converted to fp16 times `scale` on the way.
-template <bool K8, typename E>
-__device__ __forceinline__ void copy_qt(const uint8_t* src, int m, uint32_t tmem, uint32_t lane_off,
-                                        float scale) {
-#pragma unroll 1
+// TMEM).
+__device__ __forceinline__ void copy_qt(const uint8_t* src, int m, uint32_t tmem, uint32_t lane_off) {
+#pragma unroll
   for (int ch = 0; ch < 4; ++ch) {
     const uint8_t* row = src + ch * kChunkBytes + m * 128;
     uint32_t w[32];
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
       const uint4 x = *reinterpret_cast<const uint4*>(row + ((g ^ (m & 7)) << 4));
-      if constexpr (K8) {
-        w[4 * g] = to_h2_scaled<E>(x.x, scale);
-        w[4 * g + 1] = to_h2_scaled<E>(x.y, scale);
-        w[4 * g + 2] = to_h2_scaled<E>(x.z, scale);
-        w[4 * g + 3] = to_h2_scaled<E>(x.w, scale);
-      } else {
-        w[4 * g] = x.x;
-        w[4 * g + 1] = x.y;
-        w[4 * g + 2] = x.z;
-        w[4 * g + 3] = x.w;
-      }
+      w[4 * g] = x.x;
+      w[4 * g + 1] = x.y;
+      w[4 * g + 2] = x.z;
+      w[4 * g + 3] = x.w;
     }
     ptx::tmem_st32(tmem + lane_off + kColQT + 32 * ch, w);
   }
@@ -882,6 +879,109 @@ __device__ __forceinline__ void st_box_row(uint8_t* box, int m, const uint32_t (
   for (int g = 0; g < 8; ++g)
     *reinterpret_cast<uint4*>(box + m * 128 + ((g ^ (m & 7)) << 4)) =
         make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+}
+
+// FP8 variant: this thread's Q row for the kind::f8f6f4 QK^T (see Kv8).  Row m of
+// CTA `rank`'s 64 heads of virtual sequence v, read from global memory (rows past
+// the head count are zero); a = a power of two with max |q a| <= 224 (and
+// |q_pe a / s| <= 16384, s the cache's scale).  Writes hi = e4m3(q a) for all 512
+// dims to this lane's TMEM columns [kColQT, +128) (4 dims per column; both lane
+// halves hold the row), lo = e4m3(q a - hi) for this thread's half of the dims
+// (hf) to boxes 2 hf, 2 hf + 1 of the Q region (128 dims = 128 bytes a row,
+// SW128), and its half of q_pe a / s as a T hi/lo pair to boxes 4 and 5.
+// Returns s / a, the factor that takes the row's scores to their true values.
+__device__ __forceinline__ uint32_t f2_to_e4m3x2(float a, float b) {
+  return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+}
+__device__ __forceinline__ float2 e4m3x2_to_f2(uint32_t v) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(v & 0xffffu), __NV_E4M3);
+  __half2 hh;
+  hh.x = __ushort_as_half(h.x);
+  hh.y = __ushort_as_half(h.y);
+  return __half22float2(hh);
+}
+
+template <typename Out>
+__device__ __forceinline__ float quantize_q(const Params& p, int v, uint32_t rank, int m, int hf, uint8_t* qreg,
+                                            uint32_t tmem, uint32_t lane_off) {
+  const int h = vseq_head0(p, v) + 64 * (int)rank + m;
+  const bool real = h < p.heads;
+  const size_t row = (size_t)vseq_seq(p, v) * p.heads + (real ? h : 0);
+  const uint4* qg = reinterpret_cast<const uint4*>(p.q) + row * (kDim / 8);      // 8 elements a granule
+  const uint4* rg = reinterpret_cast<const uint4*>(p.qpe) + row * (kPeDim / 8);
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  float amax = 0.f, rmax = 0.f;
+#pragma unroll 1
+  for (int g = 0; g < kDim / 8; ++g) {
+    const uint4 x = real ? __ldg(qg + g) : zero;
+    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = Elt<Out>::to2(w[e]);
+      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+#pragma unroll 1
+  for (int g = 0; g < kPeDim / 8; ++g) {
+    const uint4 x = real ? __ldg(rg + g) : zero;
+    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = Elt<Out>::to2(w[e]);
+      rmax = fmaxf(rmax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+  const float s = p.kv_scale;
+  float a = amax > 0.f ? exp2f(floorf(log2f(224.f / amax))) : 1.f;
+  if (rmax * a > 16384.f * s) a = exp2f(floorf(log2f(16384.f * s / rmax)));
+  const float qs = a;
+#pragma unroll 1
+  for (int cb = 0; cb < 4; ++cb) {   // 128 dims: 32 TMEM columns, one lo box
+    uint32_t w[32];
+    uint8_t* lrow = qreg + cb * kChunkBytes + m * 128;
+    const bool mine = (cb >> 1) == hf;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) {
+      const uint4 x = real ? __ldg(qg + cb * 16 + g) : zero;
+      const uint32_t in[4] = {x.x, x.y, x.z, x.w};
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = Elt<Out>::to2(in[e]);
+        const float2 v2 = make_float2(f.x * qs, f.y * qs);
+        hi[e] = f2_to_e4m3x2(v2.x, v2.y);
+        const float2 hb = e4m3x2_to_f2(hi[e]);
+        lo[e] = f2_to_e4m3x2(v2.x - hb.x, v2.y - hb.y);
+      }
+      w[2 * g] = hi[0] | (hi[1] << 16);
+      w[2 * g + 1] = hi[2] | (hi[3] << 16);
+      if (mine)   // 8 bytes: half of 16-byte granule g / 2 (at (g / 2) ^ (m & 7))
+        *reinterpret_cast<uint2*>(lrow + (((g >> 1) ^ (m & 7)) << 4) + (g & 1) * 8) =
+            make_uint2(lo[0] | (lo[1] << 16), lo[2] | (lo[3] << 16));
+    }
+    ptx::tmem_st32(tmem + lane_off + kColQT + 32 * cb, w);
+  }
+  ptx::tmem_wait_st();
+  uint8_t* rrow = qreg + 4 * kChunkBytes + m * 128;
+  const float ra = a / s;
+#pragma unroll
+  for (int g = 4 * hf; g < 4 * hf + 4; ++g) {
+    const uint4 x = real ? __ldg(rg + g) : zero;
+    const uint32_t in[4] = {x.x, x.y, x.z, x.w};
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = Elt<Out>::to2(in[e]);
+      const float2 v2 = make_float2(f.x * ra, f.y * ra);
+      hi[e] = Elt<Out>::pack2(v2.x, v2.y);
+      const float2 hb = Elt<Out>::to2(hi[e]);
+      lo[e] = Elt<Out>::pack2(v2.x - hb.x, v2.y - hb.y);
+    }
+    const uint32_t off = (uint32_t)((g ^ (m & 7)) << 4);
+    *reinterpret_cast<uint4*>(rrow + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(rrow + kChunkBytes + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  }
+  return s / a;
 }
 
 template <typename T>
@@ -919,7 +1019,8 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
   const uint32_t s_free0_leader = ptx::mapa(ptx::smem_u32(&bars->s_free[0]), 0);
   const uint32_t p_full0_leader = ptx::mapa(ptx::smem_u32(&bars->p_full[0]), 0);
   const uint32_t o_free_leader = ptx::mapa(ptx::smem_u32(&bars->o_free), 0);
-  const float sl2 = p.sl2;
+  float sl2 = p.sl2;       // FP8: per piece, times this row's s / a
+  float qinv_next = 1.f;   // FP8: s / a of the piece whose Q was quantized last
   uint32_t gi = 0;
   uint32_t n_lx = 0, n_stg = 0, n_stg2 = 0, n_stage = 0, n_done = 0;   // barrier phases
 
@@ -938,28 +1039,22 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
     ++n_stg2;
     return ok;
   };
-  // Q dims [0, 256) of piece `k`, staged by the Q loader, into TMEM
-  auto take_qt = [&](int k) -> bool {
-    if (!wait_bar(c, qts, (uint32_t)k & 1u, kErrSoftmax)) return false;
-    copy_qt<kK8, Out>(smem + (k == 0 ? S::kP : S::kQ), m, tmem, lane_off, p.kv_scale);
-    ptx::tc_fence_before();
-    __syncwarp();
+  // Q dims [0, 256) of piece `k` (virtual sequence bb), staged by the Q loader,
+  // into TMEM.  FP8: the whole quantized Q of the piece, from global memory.
+  auto take_qt = [&](int k, int bb) -> bool {
     if constexpr (kK8) {
-      // FP8: the Q region is free for this piece's rows once every warp has copied
-      // its staged dims; then its latent dims become scaled fp16 in place
-      if (lane == 0) ptx::mbar_arrive_local(qtr);
-      if (!wait_bar(c, ptx::smem_u32(&bars->qsm), (uint32_t)k & 1u, kErrSoftmax)) return false;
-#pragma unroll 1
-      for (int i = L; i < 4 * 512; i += 128) {
-        uint4* gr = reinterpret_cast<uint4*>(smem + S::kQ + 16 * i);
-        const uint4 x = *gr;
-        *gr = make_uint4(to_h2_scaled<Out>(x.x, p.kv_scale), to_h2_scaled<Out>(x.y, p.kv_scale),
-                         to_h2_scaled<Out>(x.z, p.kv_scale), to_h2_scaled<Out>(x.w, p.kv_scale));
-      }
+      qinv_next = quantize_q<Out>(p, bb, rank, m, hf, smem + S::kQ, tmem, lane_off);
       ptx::fence_proxy_async_smem();
+      ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(qt_full_leader);
-    } else if (lane == 0) {
+      return true;
+    }
+    if (!wait_bar(c, qts, (uint32_t)k & 1u, kErrSoftmax)) return false;
+    copy_qt(smem + (k == 0 ? S::kP : S::kQ), m, tmem, lane_off);
+    ptx::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
       ptx::mbar_arrive_local(qtr);
       ptx::mbar_arrive_cluster(qt_full_leader);
     }
@@ -1041,12 +1136,13 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
   Piece pc;
   int piece = 0;
   bool have = it.next(&pc);
-  if (have && !take_qt(0)) return;
+  if (have && !take_qt(0, pc.bb)) return;
   while (have) {
     PieceIter peek = it;
     Piece nxt;
     const bool has_next = peek.next(&nxt);
     const int slen = seq_len(p, pc.bb);
+    if constexpr (kK8) sl2 = p.sl2 * qinv_next;   // this piece's scores are (a / s) x true
     float m_run = -INFINITY, l = 0.f;
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j, ++gi) {
@@ -1143,7 +1239,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(p_full0_leader + 8 * b);
       // this piece's QK^T is complete (its last S was read): the next piece's Q goes to TMEM
-      if (j == pc.end - 1 && has_next && !take_qt(piece + 1)) return;
+      if (j == pc.end - 1 && has_next && !take_qt(piece + 1, nxt.bb)) return;
     }
 
     // ---- epilogue of this piece: wait for P.V of its last tile
@@ -1348,21 +1444,18 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
   const int pair = blockIdx.x >> 1;
 
   if (threadIdx.x == 0) {
-    // operand stages: one expect-tx arrival (TMA), or FP8: 2 converter warps x 2 CTAs
-    const uint32_t n_full = Io<T>::kKv8 ? 4u : 1u;
+    // V operand stages: one expect-tx arrival (TMA), or FP8: 4 converter warps x 2 CTAs
+    const uint32_t n_vfull = Io<T>::kKv8 ? 2u * kConvWarps : 1u;
     for (int s = 0; s < 8; ++s) {
-      ptx::mbar_init(ptx::smem_u32(&bars->kfull[s]), n_full);
+      ptx::mbar_init(ptx::smem_u32(&bars->kfull[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&bars->kempty[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&bars->vfull[s]), n_full);
+      ptx::mbar_init(ptx::smem_u32(&bars->vfull[s]), n_vfull);
       ptx::mbar_init(ptx::smem_u32(&bars->vempty[s]), 1);
     }
     for (int s = 0; s < 4; ++s) {
-      ptx::mbar_init(ptx::smem_u32(&bars->k8full[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&bars->k8empty[s]), 2);
       ptx::mbar_init(ptx::smem_u32(&bars->v8full[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&bars->v8empty[s]), 2);
+      ptx::mbar_init(ptx::smem_u32(&bars->v8empty[s]), kConvWarps);
     }
-    ptx::mbar_init(ptx::smem_u32(&bars->qsm), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->q_full), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->q_empty), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->qt_full), 8);
@@ -1436,8 +1529,8 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
       wait_bar(c, ptx::smem_u32(&bars->drain_pv), 0u, kErrDrain);
     }
   } else if (Io<T>::kKv8 && warp >= 12) {
-    // FP8: warps 12, 13 convert the K stages, warps 14, 15 the V stages
-    converter<T>(p, c, pair, smem, bars, warp < 14, (warp & 1) * 32 + lane, lane);
+    // FP8: warps 12..15 dequantize the V units
+    v_converter<T>(p, c, pair, smem, bars, (warp - 12) * 32 + lane, lane);
   }
   }
   __syncwarp();
