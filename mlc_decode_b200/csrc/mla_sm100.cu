@@ -610,14 +610,14 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
 }
 
 // ---------------------------------------------------------------------------
-// FP8 variant: V converter warps (warps 12..15).  All four take every e4m3 V unit
-// (64 tokens x 128 dims, one SW128 box), each a quarter of its 16-byte granules,
+// FP8 variant: V converter warps (warps 8..15).  All eight take every e4m3 V unit
+// (64 tokens x 128 dims, one SW128 box), each an eighth of its 16-byte granules,
 // and write the fp16 operand stage P.V reads (the same rows as two SW128 boxes of
-// 64 dims); then each releases the e4m3 stage (local, count 4) and signals the
-// operand stage to the even CTA's P.V issuer (count 4 warps x 2 CTAs).  e4m3 ->
+// 64 dims); then each releases the e4m3 stage (local, count 8) and signals the
+// operand stage to the even CTA's P.V issuer (count 8 warps x 2 CTAs).  e4m3 ->
 // fp16 is exact.
 // ---------------------------------------------------------------------------
-constexpr int kConvWarps = 4;
+constexpr int kConvWarps = 8;
 
 __device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t v) {
   const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(v & 0xffffu), __NV_E4M3);
@@ -1444,7 +1444,7 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
   const int pair = blockIdx.x >> 1;
 
   if (threadIdx.x == 0) {
-    // V operand stages: one expect-tx arrival (TMA), or FP8: 4 converter warps x 2 CTAs
+    // V operand stages: one expect-tx arrival (TMA), or FP8: kConvWarps converter warps x 2 CTAs
     const uint32_t n_vfull = Io<T>::kKv8 ? 2u * kConvWarps : 1u;
     for (int s = 0; s < 8; ++s) {
       ptx::mbar_init(ptx::smem_u32(&bars->kfull[s]), 1);
@@ -1511,7 +1511,7 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
     ptx::setmaxnreg_dec<kRegsLow>();
   if (warp == 0) {
     if (lane == 0) k_producer<T>(p, c, rank, pair, sbase, bars);
-  } else if (warp == 8) {
+  } else if (warp == 8 && !Io<T>::kKv8) {
     if (lane == 0) q_loader<T>(p, c, rank, pair, sbase, bars);
   } else if (warp == 1) {
     if (rank == 0 && lane == 0) {
@@ -1521,6 +1521,8 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
       wait_bar(c, ptx::smem_u32(&bars->drain_qk), 0u, kErrDrain);
     }
   } else if (warp == 2) {
+    // (FP8: the Q loader only prefetches and never waits; it runs here first)
+    if (Io<T>::kKv8 && lane == 0) q_loader<T>(p, c, rank, pair, sbase, bars);
     if (lane == 0) v_producer<T>(p, c, rank, pair, sbase, bars);
   } else if (warp == 3) {
     if (rank == 0 && lane == 0) {
@@ -1528,9 +1530,9 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
       ptx::mma_commit_pair_mc(ptx::smem_u32(&bars->drain_pv), 0x1);
       wait_bar(c, ptx::smem_u32(&bars->drain_pv), 0u, kErrDrain);
     }
-  } else if (Io<T>::kKv8 && warp >= 12) {
-    // FP8: warps 12..15 dequantize the V units
-    v_converter<T>(p, c, pair, smem, bars, (warp - 12) * 32 + lane, lane);
+  } else if (Io<T>::kKv8 && warp >= 8) {
+    // FP8: warps 8..15 dequantize the V units
+    v_converter<T>(p, c, pair, smem, bars, (warp - 8) * 32 + lane, lane);
   }
   }
   __syncwarp();
