@@ -25,6 +25,10 @@ cpu_baseline= the oracle's restatement of the reference torch path
               (baseline_mla.py:167-191) on the host cores, on a bounded batch
               sample, scaled to the full call.
 
+``--fp8`` times the same call over an FP8 (e4m3) latent cache (mla_decode_fp8kv;
+the roofline bytes become 512 + 128 per token); ``--paged PAGE_SIZE [--ragged]``
+times the paged / variable-length entry point.
+
 ``--impl reference`` times only that reference CPU path (rank 0; other ranks
 exit without work) and prints the same line with "impl": "reference".
 """
@@ -65,6 +69,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--paged", type=int, default=0, metavar="PAGE_SIZE",
                     help="decode through mla_decode_paged with KV in shuffled pages of this many rows")
+    ap.add_argument("--fp8", action="store_true",
+                    help="decode through mla_decode_fp8kv: e4m3 latent cache (scale 1/16), rope in --dtype")
     ap.add_argument("--ragged", action="store_true",
                     help="with --paged: per-sequence lengths drawn uniformly from [1, kv_ctx] (seeded)")
     return ap.parse_args()
@@ -74,6 +80,8 @@ def workload_name(a):
     name = f"mla_decode b{a.batch}/gpu h{a.heads} s{a.kv_ctx} {a.dtype} (dim 512+64, kv_heads 1)"
     if a.paged:
         name += f", paged KV ({a.paged}-row pages" + (", ragged lengths)" if a.ragged else ")")
+    if a.fp8:
+        name += ", FP8 (e4m3) latent KV cache"
     return name
 
 
@@ -87,8 +95,9 @@ def load_peaks():
     return dict(FALLBACK_PEAKS, source="fallback")
 
 
-def algorithmic(b, h, s):
-    return b * s * 576 * 2, 2.0 * b * h * s * (576 + 512)
+def algorithmic(b, h, s, fp8=False):
+    # bytes: the latent (2 bytes a dim, or 1 for the e4m3 cache) and rope rows of every KV token
+    return b * s * (512 * (1 if fp8 else 2) + 64 * 2), 2.0 * b * h * s * (576 + 512)
 
 
 # ---------------------------------------------------------------------------
@@ -267,6 +276,23 @@ def run_ours(a, rank, world, local_rank):
 
         kern = _Paged()
         launches = 3
+    elif a.fp8:
+        base = MlaDecodeKernel(b, h, 1, s, cfg=cfg)
+        # N(0,1) latent rows stored as e4m3 codes of kv / (1/16)
+        kv = (torch.randn(b, s, 1, 512, device=dev, generator=g) * 16).clamp(-448, 448).to(torch.float8_e4m3fn)
+        k_pe = torch.randn(b, s, 1, 64, device=dev, generator=g).to(tdt)
+
+        class _Fp8:
+            def __call__(self, q_, qp_, kv_, kp_, out_):
+                base.decode_fp8(q_, qp_, kv_, kp_, 1.0 / 16, out_)
+
+            splitkv = __call__
+
+            def combine_ws(self, out_):
+                pass
+
+        kern = _Fp8()
+        launches = base.launches_per_call(tdt)
     else:
         kern = MlaDecodeKernel(b, h, 1, s, cfg=cfg)
         kv = torch.randn(b, s, 1, 512, device=dev, generator=g).to(tdt)
@@ -346,7 +372,7 @@ def run_ours(a, rank, world, local_rank):
     if rank != 0:
         return
     peaks = load_peaks()
-    bytes_alg, flops_alg = algorithmic(1, h, sum(lens))
+    bytes_alg, flops_alg = algorithmic(1, h, sum(lens), a.fp8)
     achieved = bytes_alg / (dec_us * 1e-6) / 1e9
     t_roof_us = max(bytes_alg / (peaks["hbm_gbs"] * 1e9), flops_alg / (peaks["bf16_tflops"] * 1e12)) * 1e6
     line = {
@@ -361,8 +387,9 @@ def run_ours(a, rank, world, local_rank):
                          % (bytes_alg / 1e6)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     "traffic": None if a.paged else traffic_from_profiles(a),
-                     "kernel": "paged decode call (plan + decode + combine)" if a.paged else "split-KV decode kernel",
+                     "traffic": None if (a.paged or a.fp8) else traffic_from_profiles(a),
+                     "kernel": ("paged decode call (plan + decode + combine)" if a.paged else
+                                "FP8-KV split-KV decode kernel" if a.fp8 else "split-KV decode kernel"),
                      "kernel_us": round(dec_us, 3), "peak_source": peaks["source"]},
         "mla_roofline": {"t_roof_us": round(t_roof_us, 3),
                          "frac": round(t_roof_us / us_call, 4),
@@ -376,7 +403,7 @@ def run_ours(a, rank, world, local_rank):
     }
     if a.paged:
         line["config"]["kv_rows_total"] = sum(lens)
-    if world == 1 and not a.no_cpu_baseline and not a.paged:
+    if world == 1 and not a.no_cpu_baseline and not a.paged and not a.fp8:
         times, bs, cores = cpu_time_per_call(a, a.cpu_seconds)
         cpu_us = statistics.median(times) * 1e6 * (b / bs)
         line["cpu_baseline"] = {"value": round(cpu_us, 3), "unit": UNIT, "cores": cores, "kind": "port",
