@@ -259,6 +259,20 @@ int32_t mla_decode_ext(const void* q, const void* q_pe, const void* kv_cache, co
                        int32_t max_pages_per_seq, int32_t dtype, const MlaCfg* cfg, void* stream);
 
 /*
+ * mla_decode_ext over an FP8 latent cache: kv_fp8 (same shape and paging as
+ * mla_decode_ext's kv_cache) holds e4m3 codes whose product with kv_scale is the
+ * latent row, as for mla_decode_fp8kv; k_pe_cache, q, q_pe and out stay in `dtype`.
+ * Same workspace as mla_decode_ext.  No counterpart in the reference.
+ */
+int32_t mla_decode_ext_fp8kv(const void* q, const void* q_pe, const void* kv_fp8,
+                             const void* k_pe_cache, float kv_scale, const int32_t* block_table,
+                             const int32_t* cache_seqlens, void* out, float* lse, void* workspace,
+                             size_t workspace_bytes, int32_t batch, int32_t q_len, int32_t heads,
+                             int32_t kv_heads, int32_t max_seqlen_kv, int32_t page_size,
+                             int32_t num_pages, int32_t max_pages_per_seq, int32_t dtype,
+                             const MlaCfg* cfg, void* stream);
+
+/*
  * mla_decode_fwd without a workspace argument, for callers that cannot
  * allocate device memory where they decode (code running under CUDA-graph
  * capture, servers that reserve all memory up front and forbid allocation on

@@ -27,7 +27,7 @@ EXPORTED_SYMBOLS = ("mla_abi_version", "mla_last_error", "mla_split_plan",
                     "mla_decode_combine_ws", "mla_combine", "mla_decode_fwd_noalloc",
                     "mla_describe_plan", "mla_decode_partial", "mla_paged_workspace_bytes",
                     "mla_decode_paged", "mla_decode_ext_workspace_bytes", "mla_decode_ext",
-                    "mla_decode_fp8kv")
+                    "mla_decode_fp8kv", "mla_decode_ext_fp8kv")
 
 
 class MlaCfg(ctypes.Structure):
@@ -95,6 +95,9 @@ def load(build_if_missing: bool = True):
         lib.mla_decode_fp8kv.argtypes = [vp, vp, vp, vp, ctypes.c_float, vp, vp, vp, sz, i32, i32, i32, i32,
                                          ctypes.POINTER(MlaCfg), vp]
         lib.mla_decode_fp8kv.restype = i32
+        lib.mla_decode_ext_fp8kv.argtypes = [vp, vp, vp, vp, ctypes.c_float, vp, vp, vp, vp, vp, sz, i32, i32, i32,
+                                             i32, i32, i32, i32, i32, i32, ctypes.POINTER(MlaCfg), vp]
+        lib.mla_decode_ext_fp8kv.restype = i32
         lib.mla_decode_ext_workspace_bytes.argtypes = [i32, i32, i32, i32, i32, i32, ctypes.POINTER(MlaCfg)]
         lib.mla_decode_ext_workspace_bytes.restype = sz
         lib.mla_decode_ext.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, sz, i32, i32, i32, i32, i32, i32, i32,
@@ -233,6 +236,16 @@ def decode_ext(q, q_pe, kv_cache, k_pe_cache, block_table, cache_seqlens, out, l
                                 int(batch), int(q_len), int(heads), int(kv_heads), int(max_seqlen_kv),
                                 int(page_size), int(num_pages), int(max_pages), int(dtype), ctypes.byref(cfg),
                                 stream))
+
+
+def decode_ext_fp8kv(q, q_pe, kv_fp8, k_pe_cache, kv_scale, block_table, cache_seqlens, out, lse, ws, ws_bytes,
+                     batch, q_len, heads, kv_heads, max_seqlen_kv, page_size, num_pages, max_pages, dtype,
+                     cfg: MlaCfg, stream) -> None:
+    """mla_decode_ext_fp8kv: mla_decode_ext over an e4m3 latent cache times kv_scale."""
+    check(load().mla_decode_ext_fp8kv(q, q_pe, kv_fp8, k_pe_cache, float(kv_scale), block_table, cache_seqlens, out,
+                                      lse, ws, ws_bytes, int(batch), int(q_len), int(heads), int(kv_heads),
+                                      int(max_seqlen_kv), int(page_size), int(num_pages), int(max_pages), int(dtype),
+                                      ctypes.byref(cfg), stream))
 
 
 def decode_splitkv(q, q_pe, kv, k_pe, out, lse, ws, ws_bytes, batch, heads, seqlen_kv, dtype,

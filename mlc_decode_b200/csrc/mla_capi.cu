@@ -472,7 +472,11 @@ int decode_ext(const char* fn, const void* q, const void* q_pe, const void* kv_c
                const int32_t* block_table, const int32_t* cache_seqlens, void* out, float* lse, void* workspace,
                size_t workspace_bytes, int32_t batch, int32_t q_len, int32_t heads, int32_t kv_heads,
                int32_t max_seqlen_kv, int32_t page_size, int32_t num_pages, int32_t max_pages_per_seq,
-               int32_t dtype, const MlaCfg* cfg, void* stream) {
+               int32_t dtype, const MlaCfg* cfg, void* stream, bool kv_fp8 = false, float kv_scale = 1.f) {
+  if (kv_fp8 && (!(kv_scale > 0.f) || !isfinite(kv_scale))) {
+    set_error("%s: kv_scale must be finite and > 0", fn);
+    return MLA_ERR_ARG;
+  }
   PagedLayout L;
   int rc = paged_layout(fn, batch, q_len, heads, kv_heads, max_seqlen_kv, dtype, cfg, &L);
   if (rc != MLA_OK) return rc;
@@ -510,6 +514,8 @@ int decode_ext(const char* fn, const void* q, const void* q_pe, const void* kv_c
   a.heads = heads;
   a.q_len = q_len;
   a.kv_heads = kv_heads;
+  a.kv_fp8 = kv_fp8 ? 1 : 0;
+  a.kv_scale = kv_scale;
   a.seqlen_kv = max_seqlen_kv;
   a.dtype = dtype;
   a.softmax_scale = (cfg != nullptr && cfg->softmax_scale != 0.f) ? cfg->softmax_scale : 1.0f / sqrtf((float)kQkDim);
@@ -567,6 +573,17 @@ int32_t mla_decode_ext(const void* q, const void* q_pe, const void* kv_cache, co
   return decode_ext("mla_decode_ext", q, q_pe, kv_cache, k_pe_cache, block_table, cache_seqlens, out, lse,
                     workspace, workspace_bytes, batch, q_len, heads, kv_heads, max_seqlen_kv, page_size, num_pages,
                     max_pages_per_seq, dtype, cfg, stream);
+}
+
+int32_t mla_decode_ext_fp8kv(const void* q, const void* q_pe, const void* kv_fp8, const void* k_pe_cache,
+                             float kv_scale, const int32_t* block_table, const int32_t* cache_seqlens, void* out,
+                             float* lse, void* workspace, size_t workspace_bytes, int32_t batch, int32_t q_len,
+                             int32_t heads, int32_t kv_heads, int32_t max_seqlen_kv, int32_t page_size,
+                             int32_t num_pages, int32_t max_pages_per_seq, int32_t dtype, const MlaCfg* cfg,
+                             void* stream) {
+  return decode_ext("mla_decode_ext_fp8kv", q, q_pe, kv_fp8, k_pe_cache, block_table, cache_seqlens, out, lse,
+                    workspace, workspace_bytes, batch, q_len, heads, kv_heads, max_seqlen_kv, page_size, num_pages,
+                    max_pages_per_seq, dtype, cfg, stream, true, kv_scale);
 }
 
 }  // extern "C"

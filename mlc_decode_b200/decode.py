@@ -319,11 +319,19 @@ class MlaPagedDecodeKernel:
             return 0
         return int(ws[:4].view(torch.int32).item())
 
-    def __call__(self, q, q_pe, kv_cache, k_pe_cache, cache_seqlens, out, lse=None, block_table=None):
+    def __call__(self, q, q_pe, kv_cache, k_pe_cache, cache_seqlens, out, lse=None, block_table=None,
+                 kv_scale=None):
+        """``kv_cache`` may also be an FP8 latent cache (``torch.float8_e4m3fn``, or its bytes
+        as ``torch.uint8``) of e4m3 codes whose product with ``kv_scale`` is the latent row
+        (mla_decode_ext_fp8kv); ``k_pe_cache`` stays in the model dtype."""
         b, h, smax, ql, kvh = self.batch, self.heads, self.max_seqlen_kv, self.q_len, self.kv_heads
         dtype = q.dtype if isinstance(q, torch.Tensor) else None
         if dtype not in _DTYPES:
             raise ValueError(f"q must be float16 or bfloat16, got {dtype}")
+        fp8 = isinstance(kv_cache, torch.Tensor) and kv_cache.dtype in (torch.uint8, _FP8)
+        if fp8 and kv_scale is None:
+            raise ValueError("an FP8 kv_cache needs kv_scale")
+        kv_dtype = kv_cache.dtype if fp8 else dtype
         dev = q.device
         qshape = (b, h) if ql == 1 else (b, ql, h)
         _check_tensor("q", q, (*qshape, DIM), dtype, None)
@@ -334,14 +342,14 @@ class MlaPagedDecodeKernel:
             _check_tensor("cache_seqlens", cache_seqlens, (b,), torch.int32, dev)
             sl_ptr = cache_seqlens.data_ptr()
         if block_table is None:
-            _check_tensor("kv_cache", kv_cache, (b, smax, kvh, DIM), dtype, dev)
+            _check_tensor("kv_cache", kv_cache, (b, smax, kvh, DIM), kv_dtype, dev)
             _check_tensor("k_pe_cache", k_pe_cache, (b, smax, kvh, PE_DIM), dtype, dev)
             bt_ptr, page_size, num_pages, max_pages = None, 0, 0, 0
         else:
             if kv_cache.dim() != 4:
                 raise ValueError(f"kv_cache must be [num_pages, page_size, {kvh}, 512]")
             num_pages, page_size = int(kv_cache.shape[0]), int(kv_cache.shape[1])
-            _check_tensor("kv_cache", kv_cache, (num_pages, page_size, kvh, DIM), dtype, dev)
+            _check_tensor("kv_cache", kv_cache, (num_pages, page_size, kvh, DIM), kv_dtype, dev)
             _check_tensor("k_pe_cache", k_pe_cache, (num_pages, page_size, kvh, PE_DIM), dtype, dev)
             if block_table.dim() != 2 or block_table.shape[0] != b:
                 raise ValueError(f"block_table must be [batch, max_pages], got {tuple(block_table.shape)}")
@@ -355,6 +363,12 @@ class MlaPagedDecodeKernel:
         ws = self._workspace(dev, dtype)
         with torch.cuda.device(dev):
             stream = torch.cuda.current_stream(dev).cuda_stream
-        capi.decode_ext(q.data_ptr(), q_pe.data_ptr(), kv_cache.data_ptr(), k_pe_cache.data_ptr(), bt_ptr, sl_ptr,
-                        out.data_ptr(), lse_ptr, ws.data_ptr(), ws.numel(), b, ql, h, kvh, smax, page_size,
-                        num_pages, max_pages, _DTYPES[dtype], self._ccfg, stream)
+        if fp8:
+            capi.decode_ext_fp8kv(q.data_ptr(), q_pe.data_ptr(), kv_cache.data_ptr(), k_pe_cache.data_ptr(),
+                                  float(kv_scale), bt_ptr, sl_ptr, out.data_ptr(), lse_ptr, ws.data_ptr(), ws.numel(),
+                                  b, ql, h, kvh, smax, page_size, num_pages, max_pages, _DTYPES[dtype], self._ccfg,
+                                  stream)
+        else:
+            capi.decode_ext(q.data_ptr(), q_pe.data_ptr(), kv_cache.data_ptr(), k_pe_cache.data_ptr(), bt_ptr,
+                            sl_ptr, out.data_ptr(), lse_ptr, ws.data_ptr(), ws.numel(), b, ql, h, kvh, smax,
+                            page_size, num_pages, max_pages, _DTYPES[dtype], self._ccfg, stream)
