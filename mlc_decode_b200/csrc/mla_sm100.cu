@@ -143,6 +143,7 @@ struct Cfg<Kv8<T>> {
   static constexpr int kVStages = 3;                 // fp16 V operand stages (16 KB)
   static constexpr int kV8Stages = 3;                // e4m3 V units as loaded (8 KB)
   using PT = __half;
+  static_assert(kV8Stages <= 8, "barrier arrays");
 };
 template <typename K>
 constexpr int threads_of() { return Io<K>::kKv8 ? 512 : 384; }
@@ -150,7 +151,7 @@ constexpr int threads_of() { return Io<K>::kKv8 ? 512 : 384; }
 struct Barriers {
   uint64_t kfull[8], kempty[8];
   uint64_t vfull[8], vempty[8];
-  uint64_t v8full[4], v8empty[4];   // FP8 variant: e4m3 V units as loaded
+  uint64_t v8full[8], v8empty[8];   // FP8 variant: e4m3 V units as loaded
   uint64_t q_full, q_empty, qt_full;
   uint64_t s_full[2], s_free[2];
   uint64_t p_full[2];
@@ -1452,7 +1453,7 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
       ptx::mbar_init(ptx::smem_u32(&bars->vfull[s]), n_vfull);
       ptx::mbar_init(ptx::smem_u32(&bars->vempty[s]), 1);
     }
-    for (int s = 0; s < 4; ++s) {
+    for (int s = 0; s < 8; ++s) {
       ptx::mbar_init(ptx::smem_u32(&bars->v8full[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&bars->v8empty[s]), kConvWarps);
     }
