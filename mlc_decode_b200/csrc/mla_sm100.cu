@@ -38,6 +38,16 @@
 //  * Every wait is bounded (about 2 s of %globaltimer); on timeout the CTA
 //    pair raises an abort flag, records a status code in the workspace and
 //    winds down (no trap, no hang).
+//  * FP8 KV cache (Kv8<T>): the latent cache is e4m3 with one per-tensor scale
+//    s (true value = s x code); the rope cache stays T.  QK^T runs as
+//    kind::f8f6f4 UMMAs straight from the e4m3 K tiles (8 KB stages): q is
+//    multiplied by a per-row power of two a and quantised to an e4m3 hi/lo
+//    pair (hi in TMEM, lo in shared memory), and the rope part of q carries
+//    a/s as a T hi/lo pair, so every score comes out scaled by a/s and the
+//    softmax folds s/a into its log2 scale.  For P.V the e4m3 V tiles are
+//    loaded locally and widened to fp16 by eight converter warps (warps
+//    8..15) into the fp16 operand ring; P is fp16 and the output is scaled
+//    by s in the epilogue.
 #include <cuda.h>
 #include <cuda_fp8.h>
 #include <cudaTypedefs.h>
@@ -78,7 +88,7 @@ constexpr double kWholeSlack = 10.0;  // tiles per pair a whole-sequence assignm
 // A merge stages another pair's 64 partial rows (fp32, 2 KB each) in shared memory
 // at this row pitch (16 bytes of padding: threads reading one column of 32 rows
 // hit distinct banks).
-constexpr uint32_t kMergePitch = kDim * 4 + 16;     // L2 prefetch distance of the K producer, in tiles (0: off)
+constexpr uint32_t kMergePitch = kDim * 4 + 16;
 
 // status codes written to the workspace status word on a timeout
 constexpr uint32_t kErrKLoad = 0x101, kErrVLoad = 0x102, kErrQK = 0x103, kErrPV = 0x104,
@@ -1427,7 +1437,8 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
 // ---------------------------------------------------------------------------
 // the kernel: warp 0 K producer, warp 1 TMEM owner + QK^T issuer, warp 2 V
 // producer, warp 3 P.V issuer, warps 4..7 softmax/epilogue, warp 8 Q loader
-// (warps 9..11 complete the third warpgroup)
+// (warps 9..11 complete the third warpgroup).  For an FP8 cache the block has
+// 16 warps: warp 2 also prefetches Q, and warps 8..15 convert V to fp16.
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_of<T>(), 1)
