@@ -293,6 +293,24 @@ int32_t mla_decode_fwd_noalloc(const void* q, const void* q_pe, const void* kv,
                                int32_t batch, int32_t heads, int32_t seqlen_kv,
                                int32_t dtype, const MlaCfg* cfg, void* stream);
 
+/*
+ * Self-test of the tensor-core kernel's failure detection, for tests and health
+ * checks; no reference counterpart (the reference's kernels have no bounded waits).
+ * Every wait of the decode kernel on a barrier is bounded: after about 2 s it
+ * raises an abort flag in both CTAs of its pair, records a code in the
+ * workspace's status word (MLA_ERR_DEVICE territory: 0x101..0x106 by role) and
+ * the pair winds down, so a stalled pipeline ends the kernel instead of hanging
+ * the GPU.  This call runs that same wait code in one CTA pair on barriers that
+ * nothing arrives on, faulting nothing: CTA 0 gives up after limit_ns (1e6..1e8)
+ * and writes MLA_SELFTEST_STATUS to *status (device memory, zero before the
+ * call); CTA 1 waits with 100 x the limit and must leave through the abort flag.
+ * result (device, 4 x uint64): [CTA 0 gave up (1), its wait in ns, CTA 1 left
+ * (1), its wait in ns].  Enqueues one launch; synchronize before reading.
+ */
+#define MLA_SELFTEST_STATUS 0x1ffu
+int32_t mla_selftest_wait_timeout(uint32_t* status, uint64_t* result, uint64_t limit_ns,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

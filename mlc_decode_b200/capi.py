@@ -27,7 +27,9 @@ EXPORTED_SYMBOLS = ("mla_abi_version", "mla_last_error", "mla_split_plan",
                     "mla_decode_combine_ws", "mla_combine", "mla_decode_fwd_noalloc",
                     "mla_describe_plan", "mla_decode_partial", "mla_paged_workspace_bytes",
                     "mla_decode_paged", "mla_decode_ext_workspace_bytes", "mla_decode_ext",
-                    "mla_decode_fp8kv", "mla_decode_ext_fp8kv")
+                    "mla_decode_fp8kv", "mla_decode_ext_fp8kv", "mla_selftest_wait_timeout")
+
+MLA_SELFTEST_STATUS = 0x1FF   # status word written by mla_selftest_wait_timeout
 
 
 class MlaCfg(ctypes.Structure):
@@ -98,6 +100,8 @@ def load(build_if_missing: bool = True):
         lib.mla_decode_ext_fp8kv.argtypes = [vp, vp, vp, vp, ctypes.c_float, vp, vp, vp, vp, vp, sz, i32, i32, i32,
                                              i32, i32, i32, i32, i32, i32, ctypes.POINTER(MlaCfg), vp]
         lib.mla_decode_ext_fp8kv.restype = i32
+        lib.mla_selftest_wait_timeout.argtypes = [vp, vp, ctypes.c_uint64, vp]
+        lib.mla_selftest_wait_timeout.restype = i32
         lib.mla_decode_ext_workspace_bytes.argtypes = [i32, i32, i32, i32, i32, i32, ctypes.POINTER(MlaCfg)]
         lib.mla_decode_ext_workspace_bytes.restype = sz
         lib.mla_decode_ext.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, sz, i32, i32, i32, i32, i32, i32, i32,
@@ -215,6 +219,12 @@ def decode_fp8kv(q, q_pe, kv_fp8, k_pe, kv_scale, out, lse, ws, ws_bytes, batch,
     """mla_decode_fp8kv: e4m3 latent KV rows times kv_scale (pointers are device addresses)."""
     check(load().mla_decode_fp8kv(q, q_pe, kv_fp8, k_pe, float(kv_scale), out, lse, ws, ws_bytes, int(batch),
                                   int(heads), int(seqlen_kv), int(dtype), ctypes.byref(cfg), stream))
+
+
+def selftest_wait_timeout(status, result, limit_ns, stream) -> None:
+    """mla_selftest_wait_timeout: the decode kernel's bounded-wait path run on barriers
+    nothing arrives on (status: device uint32 word, zero before; result: device 4 x uint64)."""
+    check(load().mla_selftest_wait_timeout(status, result, int(limit_ns), stream))
 
 
 def ext_workspace_bytes(batch, q_len, heads, kv_heads, max_seqlen_kv, dtype, cfg: MlaCfg) -> int:

@@ -396,6 +396,25 @@ int32_t mla_combine(const float* part_lse, const float* part_o, int32_t num_spli
   return MLA_OK;
 }
 
+int32_t mla_selftest_wait_timeout(uint32_t* status, uint64_t* result, uint64_t limit_ns, void* stream) {
+  if (!status || !result) {
+    set_error("mla_selftest_wait_timeout: null pointer");
+    return MLA_ERR_ARG;
+  }
+  if (limit_ns < 1000000ull || limit_ns > 100000000ull) {
+    set_error("mla_selftest_wait_timeout: limit_ns must be in [1e6, 1e8] (got %llu)",
+              (unsigned long long)limit_ns);
+    return MLA_ERR_ARG;
+  }
+  const cudaError_t err = launch_wait_selftest(status, reinterpret_cast<unsigned long long*>(result), limit_ns,
+                                               MLA_SELFTEST_STATUS, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) {
+    set_error("mla_selftest_wait_timeout: launch failed: %s", cudaGetErrorString(err));
+    return MLA_ERR_CUDA;
+  }
+  return MLA_OK;
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------

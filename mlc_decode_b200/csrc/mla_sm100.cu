@@ -245,14 +245,15 @@ __device__ __forceinline__ void raise_abort(const Ctx& c, uint32_t code) {
 
 // Slow path of wait_bar: poll with a time limit.  (Inlined: a call out of a
 // setmaxnreg region would have to follow the kernel-wide register budget.)
-__device__ __forceinline__ bool wait_bar_slow(const Ctx& c, uint32_t bar, uint32_t parity, uint32_t code) {
+__device__ __forceinline__ bool wait_bar_slow(const Ctx& c, uint32_t bar, uint32_t parity, uint32_t code,
+                                              uint64_t limit_ns = kTimeoutNs) {
   const uint64_t t0 = ptx::globaltimer();
   for (;;) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (ptx::mbar_try_wait(bar, parity)) return true;
     if (*reinterpret_cast<volatile uint32_t*>(c.abort_local) != 0u) return false;
-    if (ptx::globaltimer() - t0 > kTimeoutNs) {
+    if (ptx::globaltimer() - t0 > limit_ns) {
       raise_abort(c, code);
       return false;
     }
@@ -1564,6 +1565,42 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
 }
 
 // ---------------------------------------------------------------------------
+// Self-test of the timeout path (faults nothing, hangs nothing): in one CTA pair
+// each CTA's thread 0 waits, through wait_bar_slow, on an mbarrier of its own that
+// nothing ever arrives on.  CTA 0 gives up after limit_ns and takes the path every
+// role of the decode kernel takes on a timeout: abort flags raised in both CTAs,
+// `code` recorded in the status word.  CTA 1 waits with 100 x the limit and must
+// leave early through the abort flag its peer raised.  result[2 r] = 1 when CTA
+// r's wait returned false, result[2 r + 1] = how long it waited (ns).
+// ---------------------------------------------------------------------------
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(32, 1)
+mla_wait_selftest_kernel(uint32_t* status, unsigned long long* result, uint64_t limit_ns, uint32_t code) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t abort_flag;
+  const uint32_t rank = ptx::cluster_ctarank();
+  const uint32_t bar_addr = ptx::smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(bar_addr, 1);
+    abort_flag = 0u;
+    ptx::fence_mbarrier_init();
+  }
+  ptx::cluster_sync();
+  Ctx c;
+  c.abort_local = &abort_flag;
+  c.abort_peer = ptx::mapa(ptx::smem_u32(&abort_flag), rank ^ 1u);
+  c.status = status;
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = ptx::globaltimer();
+    const bool ok = wait_bar_slow(c, bar_addr, 0u, code, rank == 0 ? limit_ns : 100 * limit_ns);
+    result[2 * rank] = ok ? 0ull : 1ull;
+    result[2 * rank + 1] = (unsigned long long)(ptx::globaltimer() - t0);
+  }
+  // the peer's abort flag is written through the cluster window: both CTAs stay
+  // resident until both have finished
+  ptx::cluster_sync();
+}
+
+// ---------------------------------------------------------------------------
 // combine launch for sequences split between more pairs than the kernel above
 // merges itself (fuse_max): one 128-thread CTA per (head, sequence), 4 columns per
 // thread; other sequences were written by the decode kernel and are skipped.
@@ -1944,6 +1981,12 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
     mla_sm100_decode_kernel<__half>
         <<<2 * pairs, threads_of<__half>(), Smem<__half>::kBytes, a.stream>>>(p);
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_wait_selftest(uint32_t* status, unsigned long long* result, uint64_t limit_ns,
+                                 uint32_t code, cudaStream_t stream) {
+  sm100::mla_wait_selftest_kernel<<<2, 32, 0, stream>>>(status, result, limit_ns, code);
   return cudaGetLastError();
 }
 

@@ -31,4 +31,8 @@ cudaError_t launch_sm100_ragged_plan(const DecodeArgs& a);
 // Enqueue the combine of split sequences the decode kernel did not merge itself.
 cudaError_t launch_sm100_combine(const DecodeArgs& a);
 
+// Enqueue the bounded-wait self-test (one CTA pair; see mla_selftest_wait_timeout).
+cudaError_t launch_wait_selftest(uint32_t* status, unsigned long long* result, uint64_t limit_ns,
+                                 uint32_t code, cudaStream_t stream);
+
 }  // namespace mla
