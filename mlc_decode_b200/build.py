@@ -4,10 +4,14 @@
 source of the package for ``sm_100a`` into objects under ``_build/`` and links
 them into ``mlc_decode_b200/libmla_decode_b200.so``, next to this file, so the
 library travels with the source tree.  It rebuilds only when a source or
-header is newer than the library.
+header is newer than the library.  Concurrent builders (several ranks or test
+processes importing the package at once) take turns on a lock file in
+``_build/``; a builder that gets the lock after another finished finds the
+library up to date and returns.
 """
 from __future__ import annotations
 
+import fcntl
 import glob
 import os
 import shutil
@@ -55,8 +59,19 @@ def build(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
     """Compile (if needed) and return the path of the shared library."""
     if not force and up_to_date():
         return LIB_PATH
-    nvcc = nvcc_path()
     os.makedirs(BUILD_DIR, exist_ok=True)
+    with open(os.path.join(BUILD_DIR, ".lock"), "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        try:
+            if not force and up_to_date():   # another process built it meanwhile
+                return LIB_PATH
+            return _build_locked(verbose, extra_flags)
+        finally:
+            fcntl.flock(lock, fcntl.LOCK_UN)
+
+
+def _build_locked(verbose, extra_flags) -> str:
+    nvcc = nvcc_path()
     extra = list(extra_flags or [])
 
     def compile_one(src):
