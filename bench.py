@@ -33,7 +33,12 @@ cpu_baseline= the oracle's restatement of the reference torch path
 
 ``--fp8`` times the same call over an FP8 (e4m3) latent cache (mla_decode_fp8kv;
 the roofline bytes become 512 + 128 per token); ``--paged PAGE_SIZE [--ragged]``
-times the paged / variable-length entry point.
+times the paged / variable-length entry point.  ``--seq-split`` times BASELINE
+configs[4b] (defaults b1 h128 kv_ctx 131072): under torchrun every rank holds
+kv_ctx / N rows of each sequence, a step is its partial decode, the NCCL
+all-gather of every rank's (O, LSE) and the LSE merge (``SequenceSplitDecoder``;
+scaling "strong": the whole job is one call); with one GPU it is the plain call
+on the whole sequence.  The roofline then counts one GPU's share of the rows.
 
 ``--impl reference`` times only that reference CPU path (rank 0; other ranks
 exit without work) and prints the same line with "impl": "reference".
@@ -63,9 +68,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=64, help="sequences per GPU")
+    ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (64; --seq-split: 1)")
     ap.add_argument("--heads", type=int, default=128)
-    ap.add_argument("--kv-ctx", type=int, default=8192)
+    ap.add_argument("--kv-ctx", type=int, default=None, help="KV rows per sequence (8192; --seq-split: 131072)")
     ap.add_argument("--dtype", choices=["bf16", "fp16"], default="bf16")
     ap.add_argument("--kernel", choices=["auto", "tc", "simt"], default="auto")
     ap.add_argument("--num-split", type=int, default=0)
@@ -79,7 +84,17 @@ def parse_args():
                     help="decode through mla_decode_fp8kv: e4m3 latent cache (scale 1/16), rope in --dtype")
     ap.add_argument("--ragged", action="store_true",
                     help="with --paged: per-sequence lengths drawn uniformly from [1, kv_ctx] (seeded)")
-    return ap.parse_args()
+    ap.add_argument("--seq-split", action="store_true",
+                    help="BASELINE configs[4b]: every sequence's KV rows split across the ranks, "
+                         "(O, LSE) all-gathered over NCCL and merged")
+    a = ap.parse_args()
+    if a.batch is None:
+        a.batch = 1 if a.seq_split else 64
+    if a.kv_ctx is None:
+        a.kv_ctx = 131072 if a.seq_split else 8192
+    if a.seq_split and (a.paged or a.fp8):
+        ap.error("--seq-split takes neither --paged nor --fp8")
+    return a
 
 
 def workload_name(a):
@@ -88,6 +103,9 @@ def workload_name(a):
         name += f", paged KV ({a.paged}-row pages" + (", ragged lengths)" if a.ragged else ")")
     if a.fp8:
         name += ", FP8 (e4m3) latent KV cache"
+    if a.seq_split:
+        name = (f"mla_decode b{a.batch} h{a.heads} s{a.kv_ctx} {a.dtype} (dim 512+64, kv_heads 1), "
+                f"KV rows split across {a.gpus} GPU(s), (O, LSE) merged over NCCL")
     return name
 
 
@@ -207,7 +225,8 @@ def run_reference(a, rank):
               f"{len(times)} steps, scaled x{a.batch / bs:g} to the full call")
     line = {"impl": "reference", "metric": METRIC, "value": round(us, 3), "unit": UNIT,
             "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
-            "ms_per_step": round(us / 1000, 3), "higher_is_better": False, "scaling": "weak",
+            "ms_per_step": round(us / 1000, 3), "higher_is_better": False,
+            "scaling": "strong" if a.seq_split else "weak",
             "vs_baseline": None, "dtype": a.dtype, "data": "synthetic N(0,1), seeded",
             "config": {"workload": workload_name(a), "batch_per_gpu": a.batch, "heads": a.heads,
                        "kv_ctx": a.kv_ctx, "parallelism": "reference CPU path, host cores"},
@@ -300,6 +319,30 @@ def run_ours(a, rank, world, local_rank):
 
         kern = _Fp8()
         launches = base.launches_per_call(tdt)
+    elif a.seq_split and world > 1:
+        from mlc_decode_b200.dist import SequenceSplitDecoder
+
+        # every rank decodes the same queries against its own rows of the sequences
+        gq = torch.Generator(device=dev).manual_seed(1234)
+        q = torch.randn(b, h, 512, device=dev, generator=gq).to(tdt)
+        q_pe = torch.randn(b, h, 64, device=dev, generator=gq).to(tdt)
+        dec = SequenceSplitDecoder(b, h, s, cfg=cfg)
+        lens = [dec.local_len] * b
+        kv = torch.randn(b, dec.local_len, 1, 512, device=dev, generator=g).to(tdt)
+        k_pe = torch.randn(b, dec.local_len, 1, 64, device=dev, generator=g).to(tdt)
+
+        class _Seq:
+            def __call__(self, q_, qp_, kv_, kp_, out_):
+                dec(q_, qp_, kv_, kp_, out_)
+
+            def splitkv(self, q_, qp_, kv_, kp_, out_):
+                dec.local(q_, qp_, kv_, kp_)       # this rank's partial decode
+
+            def combine_ws(self, out_):
+                dec.merge(out_)                    # NCCL all-gather of (O, LSE) + merge
+
+        kern = _Seq()
+        launches = (dec.kernel.launches_per_call(tdt) if dec.kernel is not None else 0) + 1
     else:
         kern = MlaDecodeKernel(b, h, 1, s, cfg=cfg)
         kv = torch.randn(b, s, 1, 512, device=dev, generator=g).to(tdt)
@@ -391,11 +434,13 @@ def run_ours(a, rank, world, local_rank):
     line = {
         "metric": METRIC, "value": round(us_call, 3), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": a.warmup, "ms_per_step": round(us_call / 1000.0, 5), "higher_is_better": False,
-        "scaling": "weak", "vs_baseline": None, "dtype": a.dtype,
+        "scaling": "strong" if a.seq_split else "weak", "vs_baseline": None, "dtype": a.dtype,
         "data": "synthetic N(0,1), seeded, generated on device",
         "config": {"workload": workload_name(a), "batch_per_gpu": b, "global_batch": b * world,
                    "heads": h, "kv_ctx": s, "kernel": a.kernel, "num_split": a.num_split or "auto",
-                   "parallelism": f"batch split over {world} GPU(s), no collective",
+                   "parallelism": (f"sequence split over {world} GPU(s): NCCL all-gather of (O, LSE), "
+                                   "LSE merge" if a.seq_split and world > 1 else
+                                   f"batch split over {world} GPU(s), no collective"),
                    "l2": "inputs (KV+K_pe %.0f MB per GPU) larger than the 126 MB L2; no flush"
                          % (bytes_alg / 1e6)},
         "roofline": {"bound": "tensor" if tensor_bound else "hbm",
@@ -407,9 +452,11 @@ def run_ours(a, rank, world, local_rank):
                              "frac": round(achieved / peaks["hbm_gbs"], 4)},
                      "tensor": {"achieved_tflops": round(achieved_tc, 1), "peak_tflops": tc_peak,
                                 "peak_kind": "sustained", "frac": round(achieved_tc / tc_peak, 4)},
-                     "traffic": None if (a.paged or a.fp8) else traffic_from_profiles(a),
+                     "traffic": None if (a.paged or a.fp8 or a.seq_split) else traffic_from_profiles(a),
                      "kernel": ("paged decode call (plan + decode + combine)" if a.paged else
-                                "FP8-KV split-KV decode kernel" if a.fp8 else "split-KV decode kernel"),
+                                "FP8-KV split-KV decode kernel" if a.fp8 else
+                                "partial decode of this GPU's KV rows" if a.seq_split and world > 1 else
+                                "split-KV decode kernel"),
                      "kernel_us": round(dec_us, 3), "peak_source": peaks["source"]},
         "mla_roofline": {"t_roof_us": round(t_roof_us, 3),
                          "frac": round(t_roof_us / us_call, 4),
@@ -423,8 +470,8 @@ def run_ours(a, rank, world, local_rank):
         "gpu_launches": K * launches,
         "clocks": clk,
     }
-    if a.paged:
-        line["config"]["kv_rows_total"] = sum(lens)
+    if a.paged or a.seq_split:
+        line["config"]["kv_rows_total" if a.paged else "kv_rows_per_gpu"] = sum(lens)
     if world == 1 and not a.no_cpu_baseline and not a.paged and not a.fp8:
         times, bs, cores = cpu_time_per_call(a, a.cpu_seconds)
         cpu_us = statistics.median(times) * 1e6 * (b / bs)

@@ -81,9 +81,10 @@ class SequenceSplitDecoder:
         self.start, self.end = seq_shard(self.seqlen_kv, self.rank, self.world)
         self.local_len = self.end - self.start
         self._partial = partial_fn
+        self.kernel = None   # the MlaDecodeKernel of this rank's part (CUDA kernels only)
         if self._partial is None and self.local_len > 0:
-            kern = MlaDecodeKernel(self.batch, self.heads, 1, self.local_len, cfg=cfg)
-            self._partial = kern.partial
+            self.kernel = MlaDecodeKernel(self.batch, self.heads, 1, self.local_len, cfg=cfg)
+            self._partial = self.kernel.partial
         self._combine = combine_fn or combine
         self._bufs = {}
 
@@ -100,21 +101,30 @@ class SequenceSplitDecoder:
         return self._bufs[key]
 
     def __call__(self, q, q_pe, kv_part, k_pe_part, out, lse=None):
+        self.local(q, q_pe, kv_part, k_pe_part)
+        self.merge(out, lse, q.device)
+
+    def local(self, q, q_pe, kv_part, k_pe_part):
+        """This rank's part: normalised float32 O and LSE of its KV rows."""
         b, h = self.batch, self.heads
         if tuple(q.shape) != (b, h, DIM):
             raise ValueError(f"q has shape {tuple(q.shape)}, expected {(b, h, DIM)}")
         if kv_part.shape[1] != self.local_len or k_pe_part.shape[1] != self.local_len:
             raise ValueError(f"rank {self.rank} holds KV rows [{self.start}, {self.end}): "
                              f"expected {self.local_len} rows, got {kv_part.shape[1]}")
-        o, l, o_all, l_all = self._buffers(q.device)
+        o, l, _, _ = self._buffers(q.device)
         if self.local_len > 0:
             self._partial(q, q_pe, kv_part, k_pe_part, o, l)
         else:
             # an empty part has no mass: weight exp(-inf) = 0 in the merge
             o.zero_()
             l.fill_(float("-inf"))
+
+    def merge(self, out, lse=None, device=None):
+        """All-gather every rank's part over the process group and LSE-merge it into ``out``."""
+        b, h, w = self.batch, self.heads, self.world
+        o, l, o_all, l_all = self._buffers(device if device is not None else out.device)
         # gathered along dim 0: [world * batch, ...] is the [world, batch, ...] stack
-        w = self.world
         dist.all_gather_into_tensor(o_all.view(w * b, h, DIM), o, group=self.group)
         dist.all_gather_into_tensor(l_all.view(w * b, h), l, group=self.group)
         self._combine(l_all, o_all, out, lse)
