@@ -104,8 +104,9 @@ def workload_name(a):
     if a.fp8:
         name += ", FP8 (e4m3) latent KV cache"
     if a.seq_split:
-        name = (f"mla_decode b{a.batch} h{a.heads} s{a.kv_ctx} {a.dtype} (dim 512+64, kv_heads 1), "
-                f"KV rows split across {a.gpus} GPU(s), (O, LSE) merged over NCCL")
+        name = f"mla_decode b{a.batch} h{a.heads} s{a.kv_ctx} {a.dtype} (dim 512+64, kv_heads 1), "
+        name += (f"KV rows split across {a.gpus} GPU(s), (O, LSE) merged over NCCL" if a.gpus > 1
+                 else "whole sequence on one GPU (the sequence split's 1-GPU point)")
     return name
 
 
