@@ -98,27 +98,22 @@ mla_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   const float4* po = reinterpret_cast<const float4*>(part_o) + (size_t)row * (kDim / 4) + tid;
   const size_t split_stride = (size_t)rows * (kDim / 4);
-  int k = 0;
-  for (; k + 4 <= ns; k += 4) {
-    float4 v[4];
+  // eight partial rows in flight per thread and round (the tail rides in the last
+  // round): one L2 round trip per eight splits instead of one per split
+  for (int k = 0; k < ns; k += 8) {
+    float4 v[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = __ldg(po + (size_t)(k + u) * split_stride);
+    for (int u = 0; u < 8; ++u)
+      v[u] = k + u < ns ? __ldg(po + (size_t)(k + u) * split_stride) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 8; ++u) {
+      if (k + u >= ns) break;
       const float w = s_w[k + u];
       acc.x = fmaf(w, v[u].x, acc.x);
       acc.y = fmaf(w, v[u].y, acc.y);
       acc.z = fmaf(w, v[u].z, acc.z);
       acc.w = fmaf(w, v[u].w, acc.w);
     }
-  }
-  for (; k < ns; ++k) {
-    const float4 v = __ldg(po + (size_t)k * split_stride);
-    const float w = s_w[k];
-    acc.x = fmaf(w, v.x, acc.x);
-    acc.y = fmaf(w, v.y, acc.y);
-    acc.z = fmaf(w, v.z, acc.z);
-    acc.w = fmaf(w, v.w, acc.w);
   }
   store4<T>(out + (size_t)row * kDim + 4 * tid, acc);
   if (lse_out != nullptr && tid == 0) lse_out[row] = lse;

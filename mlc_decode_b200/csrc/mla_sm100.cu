@@ -1644,28 +1644,23 @@ mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restr
   for (int k = 0; k < n; ++k) sum += exp2f((s_lse[k] - mx) * kLog2e);
   const float lse = mx + logf(sum);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  int k = 0;
-  for (; k + 4 <= n; k += 4) {
-    float4 v[4];
+  // eight partial rows in flight per thread and round (the tail rides in the last
+  // round): one L2 round trip per eight pieces instead of one per piece
+  for (int k = 0; k < n; k += 8) {
+    float4 v[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
-      v[u] = __ldg(reinterpret_cast<const float4*>(part_o + ((size_t)s_slot[k + u] * kHeads + head) * kDim) + tid);
+    for (int u = 0; u < 8; ++u)
+      v[u] = k + u < n ? __ldg(reinterpret_cast<const float4*>(part_o + ((size_t)s_slot[k + u] * kHeads + head) * kDim) + tid)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 8; ++u) {
+      if (k + u >= n) break;
       const float w = exp2f((s_lse[k + u] - lse) * kLog2e);
       acc.x = fmaf(w, v[u].x, acc.x);
       acc.y = fmaf(w, v[u].y, acc.y);
       acc.z = fmaf(w, v[u].z, acc.z);
       acc.w = fmaf(w, v[u].w, acc.w);
     }
-  }
-  for (; k < n; ++k) {
-    const float4 v = __ldg(reinterpret_cast<const float4*>(part_o + ((size_t)s_slot[k] * kHeads + head) * kDim) + tid);
-    const float w = exp2f((s_lse[k] - lse) * kLog2e);
-    acc.x = fmaf(w, v.x, acc.x);
-    acc.y = fmaf(w, v.y, acc.y);
-    acc.z = fmaf(w, v.z, acc.z);
-    acc.w = fmaf(w, v.w, acc.w);
   }
   const int hglob = (bb % hgroups) * kHeads + head;
   if (hglob >= heads) return;   // a head past h in the last head group
