@@ -1602,9 +1602,11 @@ mla_wait_selftest_kernel(uint32_t* status, unsigned long long* result, uint64_t 
 
 // ---------------------------------------------------------------------------
 // combine launch for sequences split between more pairs than the kernel above
-// merges itself (fuse_max): one 128-thread CTA per (head, sequence), 4 columns per
-// thread; other sequences were written by the decode kernel and are skipped.
-// Same LSE algebra as mla_combine.cu (mla_decode.py:212-246).
+// merges itself (fuse_max): one CTA per (head, sequence) of kCombineGroups groups of
+// 128 threads; group g takes every kCombineGroups-th piece, 4 columns per thread and
+// eight pieces in flight per round, and the groups' sums meet in shared memory.
+// Other sequences were written by the decode kernel and are skipped.  Same LSE
+// algebra as mla_combine.cu (mla_decode.py:212-246).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void store4_out(float* dst, float4 v) { *reinterpret_cast<float4*>(dst) = v; }
 template <typename T>
@@ -1612,15 +1614,19 @@ __device__ __forceinline__ void store4_out(T* dst, float4 v) {
   *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<T>(v.x, v.y), pack2<T>(v.z, v.w));
 }
 
+constexpr int kCombineGroups = 4;
+
 template <typename OutT>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128 * kCombineGroups)
 mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__ part_o,
                         OutT* __restrict__ out, float* __restrict__ lse_out, const uint32_t* cu,
                         uint32_t total_fixed, int nt, int pairs, int vbatch, int heads, int hgroups,
                         int fuse_max) {
   __shared__ float s_lse[kMaxPairs];
   __shared__ uint32_t s_slot[kMaxPairs];
-  const int head = blockIdx.x, bb = blockIdx.y, tid = threadIdx.x;
+  __shared__ float4 s_acc[kCombineGroups - 1][128];
+  const int head = blockIdx.x, bb = blockIdx.y;
+  const int grp = threadIdx.x >> 7, tid = threadIdx.x & 127;   // piece group, column quad
   TileMap m;
   m.cu = cu;
   m.nt = (uint32_t)nt;
@@ -1632,7 +1638,7 @@ mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restr
   pairs_of_sequence(m, bb, &pf, &pl);
   const int n = pl - pf + 1;
   if (n <= fuse_max) return;   // whole, or merged by the decode kernel
-  for (int k = tid; k < n; k += 128) {
+  for (int k = threadIdx.x; k < n; k += 128 * kCombineGroups) {
     const uint32_t sl = (uint32_t)pair_slot(m, pf + k, bb);
     s_slot[k] = sl;
     s_lse[k] = __ldg(part_lse + (size_t)sl * kHeads + head);
@@ -1644,23 +1650,38 @@ mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restr
   for (int k = 0; k < n; ++k) sum += exp2f((s_lse[k] - mx) * kLog2e);
   const float lse = mx + logf(sum);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  // eight partial rows in flight per thread and round (the tail rides in the last
-  // round): one L2 round trip per eight pieces instead of one per piece
-  for (int k = 0; k < n; k += 8) {
+  // pieces grp, grp + G, grp + 2G, ...: eight partial rows in flight per thread and
+  // round (the tail rides in the last round)
+  constexpr int G = kCombineGroups;
+  for (int k0 = grp; k0 < n; k0 += 8 * G) {
     float4 v[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u)
-      v[u] = k + u < n ? __ldg(reinterpret_cast<const float4*>(part_o + ((size_t)s_slot[k + u] * kHeads + head) * kDim) + tid)
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int u = 0; u < 8; ++u) {
+      const int k = k0 + u * G;
+      v[u] = k < n ? __ldg(reinterpret_cast<const float4*>(part_o + ((size_t)s_slot[k] * kHeads + head) * kDim) + tid)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      if (k + u >= n) break;
-      const float w = exp2f((s_lse[k + u] - lse) * kLog2e);
+      const int k = k0 + u * G;
+      if (k >= n) break;
+      const float w = exp2f((s_lse[k] - lse) * kLog2e);
       acc.x = fmaf(w, v[u].x, acc.x);
       acc.y = fmaf(w, v[u].y, acc.y);
       acc.z = fmaf(w, v[u].z, acc.z);
       acc.w = fmaf(w, v[u].w, acc.w);
     }
+  }
+  if (grp > 0) s_acc[grp - 1][tid] = acc;
+  __syncthreads();
+  if (grp > 0) return;
+#pragma unroll
+  for (int g2 = 0; g2 < G - 1; ++g2) {
+    const float4 o = s_acc[g2][tid];
+    acc.x += o.x;
+    acc.y += o.y;
+    acc.z += o.z;
+    acc.w += o.w;
   }
   const int hglob = (bb % hgroups) * kHeads + head;
   if (hglob >= heads) return;   // a head past h in the last head group
@@ -1993,15 +2014,15 @@ cudaError_t launch_sm100_combine(const DecodeArgs& a) {
   const uint32_t total = (uint32_t)vb * (uint32_t)nt;
   const dim3 grid(kHeads, vb);
   if (a.out_dtype == MLA_DTYPE_F32)
-    mla_pair_combine_kernel<float><<<grid, 128, 0, a.stream>>>(
+    mla_pair_combine_kernel<float><<<grid, 128 * kCombineGroups, 0, a.stream>>>(
         a.part_lse, a.part_o, static_cast<float*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb, qs.g,
         hg, kFuseMaxPieces);
   else if (a.dtype == MLA_DTYPE_BF16)
-    mla_pair_combine_kernel<__nv_bfloat16><<<grid, 128, 0, a.stream>>>(
+    mla_pair_combine_kernel<__nv_bfloat16><<<grid, 128 * kCombineGroups, 0, a.stream>>>(
         a.part_lse, a.part_o, static_cast<__nv_bfloat16*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb,
         qs.g, hg, kFuseMaxPieces);
   else
-    mla_pair_combine_kernel<__half><<<grid, 128, 0, a.stream>>>(
+    mla_pair_combine_kernel<__half><<<grid, 128 * kCombineGroups, 0, a.stream>>>(
         a.part_lse, a.part_o, static_cast<__half*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb, qs.g,
         hg, kFuseMaxPieces);
   return cudaGetLastError();
