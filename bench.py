@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: absorbed-MLA decode, batch 64 per GPU,
+Workload (DeepSeek-V3-shaped decode): absorbed-MLA decode, batch 64 per GPU,
 128 heads, kv_len 8192, latent 512 + rope 64, bf16, N(0,1) inputs.  A step is
 one decode call ``kernel(q, q_pe, kv, k_pe, out)`` (split-KV kernel + LSE
 combine).  With N GPUs (torchrun, one rank per GPU) every rank decodes its own
@@ -16,14 +16,14 @@ value       = device time per call (us), CUDA events over exactly K steps
 roofline    = the split-KV kernel against the bound that binds it: its
               algorithmic HBM bytes (b*s*576*2) and flops (2*b*h*s*1088) per
               launch over its mean CUDA-event duration in the same timed
-              region, against MEASURED_PEAKS.json's copy bandwidth and its
-              SUSTAINED bf16 tensor rate (the timed region is thousands of
-              back-to-back calls: the part runs at its 1 kW power cap, where a
-              cuBLAS GEMM sustains 1423 of its 1687 TFLOP/s burst); "bound" is
-              whichever of the two takes longer, and both fractions are listed.
-mla_roofline= north-star fraction for the whole call: max(bytes/HBM peak,
-              flops/sustained bf16 peak) / measured us per call (the burst
-              figure's roofline is listed beside it).
+              region, against MEASURED_PEAKS.json's copy bandwidth and the bf16
+              tensor rate that applies to the clock the kernel ran at: the
+              kernel's clock probe (clock64 / %globaltimer of one CTA, summed
+              over the timed calls) gives its SM MHz; within 5 % of the maximum
+              clock the burst GEMM rate applies, below it the sustained rate
+              (the 1 kW power cap).  frac = max(T_hbm, T_tensor) / kernel time;
+              "bound" names the larger term; both fractions are listed.
+mla_roofline= the same fraction for the whole call (decode + any combine).
 e2e         = the same call through the public API with HOST buffers: pinned
               host->device copies of q, q_pe, kv, k_pe and a device->host read
               of out inside every timed step.
@@ -33,8 +33,8 @@ cpu_baseline= the oracle's restatement of the reference torch path
 
 ``--fp8`` times the same call over an FP8 (e4m3) latent cache (mla_decode_fp8kv;
 the roofline bytes become 512 + 128 per token); ``--paged PAGE_SIZE [--ragged]``
-times the paged / variable-length entry point.  ``--seq-split`` times BASELINE
-configs[4b] (defaults b1 h128 kv_ctx 131072): under torchrun every rank holds
+times the paged / variable-length entry point.  ``--seq-split`` times the long-context
+sequence split (defaults b1 h128 kv_ctx 131072): under torchrun every rank holds
 kv_ctx / N rows of each sequence, a step is its partial decode, the NCCL
 all-gather of every rank's (O, LSE) and the LSE merge (``SequenceSplitDecoder``;
 scaling "strong": the whole job is one call); with one GPU it is the plain call
@@ -67,7 +67,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (64; --seq-split: 1)")
@@ -87,7 +87,7 @@ def parse_args():
     ap.add_argument("--ragged", action="store_true",
                     help="with --paged: per-sequence lengths drawn uniformly from [1, kv_ctx] (seeded)")
     ap.add_argument("--seq-split", action="store_true",
-                    help="BASELINE configs[4b]: every sequence's KV rows split across the ranks, "
+                    help="long-context sequence split: every sequence's KV rows split across the ranks, "
                          "(O, LSE) all-gathered over NCCL and merged")
     a = ap.parse_args()
     if a.batch is None:
@@ -110,6 +110,23 @@ def workload_name(a):
         name += (f"KV rows split across {a.gpus} GPU(s), (O, LSE) merged over NCCL" if a.gpus > 1
                  else "whole sequence on one GPU (the sequence split's 1-GPU point)")
     return name
+
+
+def config_of(a, world, kv_bytes=None, flushed=None):
+    """The `config` object of the JSON line: the same keys in both arms."""
+    if kv_bytes is None:
+        per_row = 512 * (1 if a.fp8 else 2) + 64 * 2
+        kv_bytes = a.batch * a.kv_ctx * per_row // (world if a.seq_split else 1)
+    if flushed is None:
+        flushed = kv_bytes < 2 * L2_BYTES
+    return {"workload": workload_name(a), "batch_per_gpu": a.batch, "global_batch": a.batch * (1 if a.seq_split else world),
+            "heads": a.heads, "kv_ctx": a.kv_ctx, "kernel": a.kernel, "num_split": a.num_split or "auto",
+            "parallelism": (f"sequence split over {world} GPU(s): NCCL all-gather of (O, LSE), LSE merge"
+                            if a.seq_split and world > 1 else f"batch split over {world} GPU(s), no collective"),
+            "l2": ("inputs (KV+K_pe %.0f MB per GPU) larger than the 126 MB L2; no flush" % (kv_bytes / 1e6)
+                   if not flushed else
+                   "inputs (KV+K_pe %.0f MB per GPU) under twice the 126 MB L2: a 256 MB buffer "
+                   "written before every step, outside its events" % (kv_bytes / 1e6))}
 
 
 def load_peaks():
@@ -231,8 +248,7 @@ def run_reference(a, rank):
             "ms_per_step": round(us / 1000, 3), "higher_is_better": False,
             "scaling": "strong" if a.seq_split else "weak",
             "vs_baseline": None, "dtype": a.dtype, "data": "synthetic N(0,1), seeded",
-            "config": {"workload": workload_name(a), "batch_per_gpu": a.batch, "heads": a.heads,
-                       "kv_ctx": a.kv_ctx, "parallelism": "reference CPU path, host cores"},
+            "config": config_of(a, a.gpus), "arm": "reference CPU path (torch on host cores)",
             "cpu_baseline": {"value": round(us, 3), "unit": UNIT, "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(us, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -253,6 +269,26 @@ def traffic_from_profiles(a):
     ent = d.get(f"b{a.batch}_h{a.heads}_s{a.kv_ctx}_{a.dtype}_{a.kernel}") or \
         d.get(f"b{a.batch}_h{a.heads}_s{a.kv_ctx}_{a.dtype}")
     return None if ent is None else ent.get("dram_bytes_per_launch")
+
+
+def read_probe(obj, dev, dtype):
+    """(cycles, ns, calls) of the decode kernel's clock probe, or None (CUDA-core kernel)."""
+    if obj is None or not hasattr(obj, "clock_probe"):
+        return None
+    try:
+        return obj.clock_probe(dev, dtype)
+    except Exception:  # noqa: BLE001 - the probe is informational
+        return None
+
+
+def kernel_clock(p0, p1, sm_max):
+    """SM clock the decode kernel ran at inside the timed region, from its probe."""
+    if p0 is None or p1 is None or p1[2] <= p0[2] or p1[1] <= p0[1]:
+        return None
+    mhz = (p1[0] - p0[0]) / (p1[1] - p0[1]) * 1000.0
+    return {"sm_mhz": round(mhz, 1), "calls": p1[2] - p0[2],
+            "of_max": round(mhz / sm_max, 4) if sm_max else None,
+            "how": "clock64 and %globaltimer over one CTA's whole run, every call, summed"}
 
 
 def run_ours(a, rank, world, local_rank):
@@ -304,6 +340,7 @@ def run_ours(a, rank, world, local_rank):
                 pass
 
         kern = _Paged()
+        probe_obj = pkern
         launches = 3
     elif a.fp8:
         base = MlaDecodeKernel(b, h, 1, s, cfg=cfg)
@@ -321,6 +358,7 @@ def run_ours(a, rank, world, local_rank):
                 pass
 
         kern = _Fp8()
+        probe_obj = base
         launches = base.launches_per_call(tdt)
     elif a.seq_split and world > 1:
         from mlc_decode_b200.dist import SequenceSplitDecoder
@@ -345,9 +383,11 @@ def run_ours(a, rank, world, local_rank):
                 dec.merge(out_)                    # NCCL all-gather of (O, LSE) + merge
 
         kern = _Seq()
+        probe_obj = dec.kernel
         launches = (dec.kernel.launches_per_call(tdt) if dec.kernel is not None else 0) + 1
     else:
         kern = MlaDecodeKernel(b, h, 1, s, cfg=cfg)
+        probe_obj = kern
         kv = torch.randn(b, s, 1, 512, device=dev, generator=g).to(tdt)
         k_pe = torch.randn(b, s, 1, 64, device=dev, generator=g).to(tdt)
         launches = kern.launches_per_call(tdt)
@@ -375,6 +415,7 @@ def run_ours(a, rank, world, local_rank):
     ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(K)] if flush is not None else None
     barrier()
     torch.cuda.synchronize()
+    probe0 = read_probe(probe_obj, dev, tdt)
     clocks.mark(True)
     start.record()
     for i in range(K):
@@ -390,6 +431,7 @@ def run_ours(a, rank, world, local_rank):
     end.record()
     torch.cuda.synchronize()
     clocks.mark(False)
+    probe1 = read_probe(probe_obj, dev, tdt)
     barrier()
     clk = clocks.stop()
     total_ms = (start.elapsed_time(end) if flush is None else
@@ -440,48 +482,56 @@ def run_ours(a, rank, world, local_rank):
     bytes_alg, flops_alg = algorithmic(1, h, sum(lens), a.fp8)
     achieved = bytes_alg / (dec_us * 1e-6) / 1e9                 # GB/s
     achieved_tc = flops_alg / (dec_us * 1e-6) / 1e12             # TFLOP/s
-    tc_peak = peaks["bf16_tflops_sustained"]
+    sm_max = (clk or {}).get("sm_max_mhz") or 1965.0
+    kclk = kernel_clock(probe0, probe1, sm_max)
+    # Which tensor peak applies is read off the clock the kernel actually ran at:
+    # within 5 % of the maximum SM clock the part was not power-capped during the
+    # timed region (a short run), so the burst GEMM rate applies; below it, the
+    # sustained rate under the 1 kW cap.  Without a probe (CUDA-core kernel): burst
+    # for a timed region under 50 ms, else sustained.
+    if kclk is not None:
+        sustained = kclk["sm_mhz"] < 0.95 * sm_max
+    else:
+        sustained = total_ms > 50.0
+    tc_peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
     t_hbm_us = bytes_alg / (peaks["hbm_gbs"] * 1e9) * 1e6
     t_tc_us = flops_alg / (tc_peak * 1e12) * 1e6
     t_roof_us = max(t_hbm_us, t_tc_us)
-    t_roof_burst_us = max(t_hbm_us, flops_alg / (peaks["bf16_tflops"] * 1e12) * 1e6)
     tensor_bound = t_tc_us > t_hbm_us and not a.fp8   # (FP8 QK^T: not the bf16 tensor rate)
+    peak_kind = "sustained" if sustained else "burst"
     line = {
         "metric": METRIC, "value": round(us_call, 3), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": a.warmup, "ms_per_step": round(us_call / 1000.0, 5), "higher_is_better": False,
         "scaling": "strong" if a.seq_split else "weak", "vs_baseline": None, "dtype": a.dtype,
         "data": "synthetic N(0,1), seeded, generated on device",
-        "config": {"workload": workload_name(a), "batch_per_gpu": b, "global_batch": b * world,
-                   "heads": h, "kv_ctx": s, "kernel": a.kernel, "num_split": a.num_split or "auto",
-                   "parallelism": (f"sequence split over {world} GPU(s): NCCL all-gather of (O, LSE), "
-                                   "LSE merge" if a.seq_split and world > 1 else
-                                   f"batch split over {world} GPU(s), no collective"),
-                   "l2": ("inputs (KV+K_pe %.0f MB per GPU) larger than the 126 MB L2; no flush"
-                          % (kv_bytes / 1e6) if flush is None else
-                          "inputs (KV+K_pe %.0f MB per GPU) under twice the 126 MB L2: a 256 MB buffer "
-                          "written before every step, outside its events" % (kv_bytes / 1e6))},
+        "config": config_of(a, world, kv_bytes, flush is not None), "arm": "B200 CUDA kernels",
         "roofline": {"bound": "tensor" if tensor_bound else "hbm",
                      "achieved": round(achieved_tc if tensor_bound else achieved, 1),
                      "peak": tc_peak if tensor_bound else peaks["hbm_gbs"],
                      "unit": "TFLOP/s" if tensor_bound else "GB/s",
-                     "frac": round(achieved_tc / tc_peak if tensor_bound else achieved / peaks["hbm_gbs"], 4),
+                     "frac": round(t_roof_us / dec_us, 4),
+                     "peak_kind": peak_kind,
                      "hbm": {"achieved_gbs": round(achieved, 1), "peak_gbs": peaks["hbm_gbs"],
                              "frac": round(achieved / peaks["hbm_gbs"], 4)},
                      "tensor": {"achieved_tflops": round(achieved_tc, 1), "peak_tflops": tc_peak,
-                                "peak_kind": "sustained", "frac": round(achieved_tc / tc_peak, 4)},
+                                "peak_kind": peak_kind, "frac": round(achieved_tc / tc_peak, 4),
+                                "burst_peak_tflops": peaks["bf16_tflops"],
+                                "sustained_peak_tflops": peaks["bf16_tflops_sustained"]},
                      "traffic": None if (a.paged or a.fp8 or a.seq_split) else traffic_from_profiles(a),
                      "kernel": ("paged decode call (plan + decode + combine)" if a.paged else
                                 "FP8-KV split-KV decode kernel" if a.fp8 else
                                 "partial decode of this GPU's KV rows" if a.seq_split and world > 1 else
                                 "split-KV decode kernel"),
-                     "kernel_us": round(dec_us, 3), "peak_source": peaks["source"]},
-        "mla_roofline": {"t_roof_us": round(t_roof_us, 3),
+                     "kernel_us": round(dec_us, 3), "peak_source": peaks["source"],
+                     "kernel_clock": kclk,
+                     "kernel_kcycles": (round(dec_us * kclk["sm_mhz"] / 1000.0, 1) if kclk else None)},
+        "mla_roofline": {"t_roof_us": round(t_roof_us, 3), "peak_kind": peak_kind,
                          "frac": round(t_roof_us / us_call, 4),
-                         "t_roof_us_burst": round(t_roof_burst_us, 3),
-                         "frac_burst": round(t_roof_burst_us / us_call, 4),
+                         "t_hbm_us": round(t_hbm_us, 3), "t_tensor_us": round(t_tc_us, 3),
                          "hbm_bytes": bytes_alg, "flops": flops_alg,
                          "peaks": {"hbm_gbs": peaks["hbm_gbs"], "bf16_tflops": peaks["bf16_tflops"],
-                                   "bf16_tflops_sustained": tc_peak, "source": peaks["source"]}},
+                                   "bf16_tflops_sustained": peaks["bf16_tflops_sustained"],
+                                   "source": peaks["source"]}},
         "e2e": {"value": round(e2e_us, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": E},
         "gpu_launches": K * launches,

@@ -160,6 +160,20 @@ int32_t mla_combine(const float* part_lse, const float* part_o,
                     void* out, float* lse, int32_t dtype, void* stream);
 
 /*
+ * mla_combine over partials that are not split-major: split k's LSE row r is
+ * part_lse[k * lse_split_stride + r] and its O row r starts at
+ * part_o + k * o_split_stride + r * 512 (strides in floats, o_split_stride a
+ * multiple of 4).  The cross-GPU merge of the sequence split gathers every
+ * GPU's (O, LSE) as one packed block per GPU ([O | LSE | padding]) in a single
+ * all-gather and merges it in place with this call.  No reference counterpart
+ * (its partials are always split-minor in one buffer, mla_decode.py:73-76).
+ */
+int32_t mla_combine_strided(const float* part_lse, int64_t lse_split_stride,
+                            const float* part_o, int64_t o_split_stride,
+                            int32_t num_split, int32_t batch, int32_t heads,
+                            void* out, float* lse, int32_t dtype, void* stream);
+
+/*
  * mla_decode_fwd for one contiguous part of every sequence's KV cache, with a
  * float32 result: o[b,h,:] (float32 [batch, heads, 512], normalised) and
  * lse[b,h] (float32 [batch, heads], natural log, required) are the decode of
@@ -282,16 +296,38 @@ int32_t mla_decode_ext_fp8kv(const void* q, const void* q_pe, const void* kv_fp8
  * Same inputs, outputs, checks and result as mla_decode_fwd; the split-KV
  * scratch comes from a static device array of MLA_NOALLOC_SCRATCH_BYTES that
  * every GPU loading the library holds until exit.  Shapes whose
- * mla_workspace_bytes exceeds it return MLA_ERR_WORKSPACE.  The first call on
- * a device looks up the array's address (cudaGetSymbolAddress); make it
- * before any stream capture.  All calls share the array: calls that overlap
- * on the GPU race.  Allocates nothing.
+ * mla_workspace_bytes exceeds it (for the CUDA-core kernel: it plus a 256-byte
+ * status block kept in front) return MLA_ERR_WORKSPACE.  A rejected call
+ * enqueues nothing.  The array's address is looked up once per device
+ * (cudaGetSymbolAddress, with that device current) by mla_noalloc_init or by
+ * the first decode call on the device; make one of them before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race.
+ * Allocates nothing.
  */
 #define MLA_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
 int32_t mla_decode_fwd_noalloc(const void* q, const void* q_pe, const void* kv,
                                const void* k_pe, void* out, float* lse,
                                int32_t batch, int32_t heads, int32_t seqlen_kv,
                                int32_t dtype, const MlaCfg* cfg, void* stream);
+
+/*
+ * Looks up the static scratch array's address on the current device, so that a
+ * host can prepare before it captures its first decode into a CUDA graph.
+ * Optional (the first mla_decode_fwd_noalloc on the device does the same).
+ * Same reason for existing as mla_decode_fwd_noalloc; no reference counterpart.
+ */
+int32_t mla_noalloc_init(void);
+
+/*
+ * Enqueues on `stream` a copy of the status word of the static scratch array
+ * (current device) into *status_out (device or host memory): 0 after any
+ * mla_decode_fwd_noalloc call, unless that call ran the tensor-core kernel and
+ * one of its bounded waits gave up: then the code it recorded (0x101..0x106, as
+ * in mla_decode_fwd's workspace status word).  Read it after that call and
+ * before the next, which clears it.
+ * No reference counterpart.
+ */
+int32_t mla_noalloc_status(uint32_t* status_out, void* stream);
 
 /*
  * Self-test of the tensor-core kernel's failure detection, for tests and health

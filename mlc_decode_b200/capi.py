@@ -27,7 +27,8 @@ EXPORTED_SYMBOLS = ("mla_abi_version", "mla_last_error", "mla_split_plan",
                     "mla_decode_combine_ws", "mla_combine", "mla_decode_fwd_noalloc",
                     "mla_describe_plan", "mla_decode_partial", "mla_paged_workspace_bytes",
                     "mla_decode_paged", "mla_decode_ext_workspace_bytes", "mla_decode_ext",
-                    "mla_decode_fp8kv", "mla_decode_ext_fp8kv", "mla_selftest_wait_timeout")
+                    "mla_decode_fp8kv", "mla_decode_ext_fp8kv", "mla_selftest_wait_timeout",
+                    "mla_noalloc_init", "mla_noalloc_status", "mla_combine_strided")
 
 MLA_SELFTEST_STATUS = 0x1FF   # status word written by mla_selftest_wait_timeout
 
@@ -118,6 +119,12 @@ def load(build_if_missing: bool = True):
         lib.mla_describe_plan.restype = i32
         lib.mla_combine.argtypes = [vp, vp, i32, i32, i32, vp, vp, i32, vp]
         lib.mla_combine.restype = i32
+        lib.mla_combine_strided.argtypes = [vp, ctypes.c_int64, vp, ctypes.c_int64, i32, i32, i32, vp, vp, i32, vp]
+        lib.mla_combine_strided.restype = i32
+        lib.mla_noalloc_init.argtypes = []
+        lib.mla_noalloc_init.restype = i32
+        lib.mla_noalloc_status.argtypes = [vp, vp]
+        lib.mla_noalloc_status.restype = i32
         _lib = lib
         return lib
 
@@ -273,3 +280,20 @@ def decode_combine_ws(out, lse, ws, ws_bytes, batch, heads, seqlen_kv, dtype, cf
 def combine(part_lse, part_o, num_split, batch, heads, out, lse, dtype, stream) -> None:
     check(load().mla_combine(part_lse, part_o, int(num_split), int(batch), int(heads), out, lse,
                              int(dtype), stream))
+
+
+def combine_strided(part_lse, lse_stride, part_o, o_stride, num_split, batch, heads, out, lse, dtype,
+                    stream) -> None:
+    """mla_combine_strided: split k's rows at part_lse + k*lse_stride, part_o + k*o_stride (floats)."""
+    check(load().mla_combine_strided(part_lse, int(lse_stride), part_o, int(o_stride), int(num_split),
+                                     int(batch), int(heads), out, lse, int(dtype), stream))
+
+
+def noalloc_init() -> None:
+    """mla_noalloc_init: look up the static scratch array on the current device."""
+    check(load().mla_noalloc_init())
+
+
+def noalloc_status(status_out, stream) -> None:
+    """mla_noalloc_status: enqueue a copy of the static array's status word to ``status_out``."""
+    check(load().mla_noalloc_status(status_out, stream))

@@ -109,7 +109,9 @@ int resolve(int batch, int heads, int seqlen_kv, const MlaCfg* cfg, Resolved* r)
 //                       (partials only when some sequence is split between CTA pairs)
 //   CUDA-core kernel:   [partial LSE][partial O] when the plan has more than one split
 // The tensor-core kernel's counters must be zero before the first call (a zero-filled
-// workspace); every call leaves them zero again.
+// workspace); every call leaves them zero again.  The 256-byte status block holds the
+// status word (bytes 0-3) and the kernel's clock probe (uint64 SM cycles, ns and calls
+// at bytes 8, 16, 24, accumulated over calls).
 constexpr size_t kStatusBytes = 256;
 
 // one counter per (sequence, group of 128 heads, CTA rank) of the tensor-core kernel
@@ -246,6 +248,30 @@ int prepare(const char* fn, const void* q, const void* q_pe, const void* kv, con
   }
   return MLA_OK;
 }
+
+}  // namespace
+
+int check_decode_call(const char* fn, const void* q, const void* q_pe, const void* kv, const void* k_pe,
+                      const void* out, int batch, int heads, int seqlen_kv, int dtype, const MlaCfg* cfg) {
+  int rc = check_shape(batch, heads, seqlen_kv, dtype);
+  if (rc != MLA_OK) return rc;
+  if (!q || !q_pe || !kv || !k_pe || !out) {
+    set_error("%s: null tensor pointer", fn);
+    return MLA_ERR_ARG;
+  }
+  if (!aligned16(q) || !aligned16(q_pe) || !aligned16(kv) || !aligned16(k_pe) || !aligned16(out)) {
+    set_error("%s: tensor pointers must be 16-byte aligned", fn);
+    return MLA_ERR_ARG;
+  }
+  if (cfg != nullptr && cfg->softmax_scale != 0.f && (!(cfg->softmax_scale > 0.f) || !isfinite(cfg->softmax_scale))) {
+    set_error("%s: softmax_scale must be finite and > 0", fn);
+    return MLA_ERR_ARG;
+  }
+  Resolved r{};
+  return resolve(batch, heads, seqlen_kv, cfg, &r);
+}
+
+namespace {
 
 int run_splitkv(const char* fn, const DecodeArgs& a, const Resolved& r) {
   const cudaError_t err =
@@ -391,6 +417,42 @@ int32_t mla_combine(const float* part_lse, const float* part_o, int32_t num_spli
                                          static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) {
     set_error("mla_combine: launch failed: %s", cudaGetErrorString(err));
+    return MLA_ERR_CUDA;
+  }
+  return MLA_OK;
+}
+
+int32_t mla_combine_strided(const float* part_lse, int64_t lse_split_stride, const float* part_o,
+                            int64_t o_split_stride, int32_t num_split, int32_t batch, int32_t heads, void* out,
+                            float* lse, int32_t dtype, void* stream) {
+  if (!part_lse || !part_o || !out) {
+    set_error("mla_combine_strided: null pointer");
+    return MLA_ERR_ARG;
+  }
+  if (num_split < 1 || num_split > 8192 || batch < 1 || heads < 1) {
+    set_error("mla_combine_strided: bad num_split/batch/heads (%d, %d, %d)", num_split, batch, heads);
+    return MLA_ERR_ARG;
+  }
+  const int64_t rows = (int64_t)batch * heads;
+  if (lse_split_stride < rows || o_split_stride < rows * kDim || o_split_stride % 4 != 0) {
+    set_error("mla_combine_strided: split strides must cover a split (lse >= %lld, o >= %lld and a multiple "
+              "of 4; got %lld, %lld)", (long long)rows, (long long)(rows * kDim), (long long)lse_split_stride,
+              (long long)o_split_stride);
+    return MLA_ERR_ARG;
+  }
+  if (dtype != MLA_DTYPE_F16 && dtype != MLA_DTYPE_BF16 && dtype != MLA_DTYPE_F32) {
+    set_error("mla_combine_strided: dtype must be 0, 1 or 2");
+    return MLA_ERR_ARG;
+  }
+  if (!aligned16(part_o) || !aligned16(out)) {
+    set_error("mla_combine_strided: part_o and out must be 16-byte aligned");
+    return MLA_ERR_ARG;
+  }
+  const cudaError_t err = launch_combine_strided(part_lse, (size_t)lse_split_stride, part_o, (size_t)o_split_stride,
+                                                 num_split, batch, heads, out, lse, dtype,
+                                                 static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) {
+    set_error("mla_combine_strided: launch failed: %s", cudaGetErrorString(err));
     return MLA_ERR_CUDA;
   }
   return MLA_OK;

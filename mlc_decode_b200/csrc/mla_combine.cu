@@ -51,10 +51,13 @@ __device__ __forceinline__ void store4<float>(float* dst, float4 v) {
   *reinterpret_cast<float4*>(dst) = v;
 }
 
+// Split k's LSE of row r is part_lse[k * lse_stride + r], its O row starts at
+// part_o + k * o_stride + r * 512 (strides in floats; o_stride a multiple of 4).
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
 mla_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__ part_o,
-                   int ns, int rows, T* __restrict__ out, float* __restrict__ lse_out) {
+                   int ns, int rows, size_t lse_stride, size_t o_stride, T* __restrict__ out,
+                   float* __restrict__ lse_out) {
   extern __shared__ float s_w[];        // [ns] weights
   __shared__ float s_red[kThreads / 32];
   __shared__ float s_bcast;
@@ -63,7 +66,7 @@ mla_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__
   const int lane = tid & 31, warp = tid >> 5;
 
   float mx = -INFINITY;
-  for (int k = tid; k < ns; k += kThreads) mx = fmaxf(mx, part_lse[(size_t)k * rows + row]);
+  for (int k = tid; k < ns; k += kThreads) mx = fmaxf(mx, part_lse[(size_t)k * lse_stride + row]);
   mx = warp_max(mx);
   if (lane == 0) s_red[warp] = mx;
   __syncthreads();
@@ -79,7 +82,7 @@ mla_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__
 
   float sum = 0.f;
   for (int k = tid; k < ns; k += kThreads)
-    sum += exp2f((part_lse[(size_t)k * rows + row] - msafe) * kLog2e);
+    sum += exp2f((part_lse[(size_t)k * lse_stride + row] - msafe) * kLog2e);
   sum = warp_sum(sum);
   __syncthreads();
   if (lane == 0) s_red[warp] = sum;
@@ -92,12 +95,12 @@ mla_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__
   __syncthreads();
   const float lse = all_empty ? -INFINITY : msafe + logf(s_bcast);
   for (int k = tid; k < ns; k += kThreads)
-    s_w[k] = all_empty ? 0.f : exp2f((part_lse[(size_t)k * rows + row] - lse) * kLog2e);
+    s_w[k] = all_empty ? 0.f : exp2f((part_lse[(size_t)k * lse_stride + row] - lse) * kLog2e);
   __syncthreads();
 
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   const float4* po = reinterpret_cast<const float4*>(part_o) + (size_t)row * (kDim / 4) + tid;
-  const size_t split_stride = (size_t)rows * (kDim / 4);
+  const size_t split_stride = o_stride / 4;
   // eight partial rows in flight per thread and round (the tail rides in the last
   // round): one L2 round trip per eight splits instead of one per split
   for (int k = 0; k < ns; k += 8) {
@@ -121,22 +124,30 @@ mla_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__
 
 }  // namespace
 
-cudaError_t launch_combine(const float* part_lse, const float* part_o, int ns, int batch,
-                           int heads, void* out, float* lse, int dtype, cudaStream_t stream) {
-  if (ns < 1 || ns > kMaxSplits) return cudaErrorInvalidValue;
+cudaError_t launch_combine_strided(const float* part_lse, size_t lse_stride, const float* part_o,
+                                   size_t o_stride, int ns, int batch, int heads, void* out, float* lse,
+                                   int dtype, cudaStream_t stream) {
+  if (ns < 1 || ns > kMaxSplits || o_stride % 4 != 0) return cudaErrorInvalidValue;
   const int rows = batch * heads;
   const size_t smem = sizeof(float) * (size_t)ns;
   if (dtype == MLA_DTYPE_F16) {
     mla_combine_kernel<__half><<<rows, kThreads, smem, stream>>>(
-        part_lse, part_o, ns, rows, static_cast<__half*>(out), lse);
+        part_lse, part_o, ns, rows, lse_stride, o_stride, static_cast<__half*>(out), lse);
   } else if (dtype == MLA_DTYPE_F32) {
     mla_combine_kernel<float><<<rows, kThreads, smem, stream>>>(
-        part_lse, part_o, ns, rows, static_cast<float*>(out), lse);
+        part_lse, part_o, ns, rows, lse_stride, o_stride, static_cast<float*>(out), lse);
   } else {
     mla_combine_kernel<__nv_bfloat16><<<rows, kThreads, smem, stream>>>(
-        part_lse, part_o, ns, rows, static_cast<__nv_bfloat16*>(out), lse);
+        part_lse, part_o, ns, rows, lse_stride, o_stride, static_cast<__nv_bfloat16*>(out), lse);
   }
   return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const float* part_lse, const float* part_o, int ns, int batch,
+                           int heads, void* out, float* lse, int dtype, cudaStream_t stream) {
+  const size_t rows = (size_t)batch * heads;
+  return launch_combine_strided(part_lse, rows, part_o, rows * kDim, ns, batch, heads, out, lse, dtype,
+                                stream);
 }
 
 }  // namespace mla

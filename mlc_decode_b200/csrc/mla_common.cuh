@@ -101,6 +101,12 @@ __host__ __device__ __forceinline__ void split_range(int z, int bpc, int extra, 
 // ---------------------------------------------------------------------------
 void set_error(const char* fmt, ...);
 
+// Checks a decode call's shape, dtype, tensor pointers (non-null, 16-byte
+// aligned) and config exactly as mla_decode_fwd does before it launches
+// anything; MLA_OK or the status mla_decode_fwd would return (error text set).
+int check_decode_call(const char* fn, const void* q, const void* q_pe, const void* kv, const void* k_pe,
+                      const void* out, int batch, int heads, int seqlen_kv, int dtype, const MlaCfg* cfg);
+
 // ---------------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------------
@@ -147,8 +153,12 @@ cudaError_t launch_simt_decode(const DecodeArgs& a);
 int simt_block_n();                       // KV rows per tile of the SIMT kernel
 int simt_ctas_per_sm();                   // resident CTAs per SM (occupancy target)
 
-// LSE combine (mla_combine.cu).
+// LSE combine (mla_combine.cu): split-major partials, or split k's LSE rows at
+// part_lse + k * lse_stride and O rows at part_o + k * o_stride (floats).
 cudaError_t launch_combine(const float* part_lse, const float* part_o, int ns, int batch,
                            int heads, void* out, float* lse, int dtype, cudaStream_t stream);
+cudaError_t launch_combine_strided(const float* part_lse, size_t lse_stride, const float* part_o,
+                                   size_t o_stride, int ns, int batch, int heads, void* out, float* lse,
+                                   int dtype, cudaStream_t stream);
 
 }  // namespace mla

@@ -90,6 +90,9 @@ constexpr double kWholeSlack = 10.0;  // tiles per pair a whole-sequence assignm
 // hit distinct banks).
 constexpr uint32_t kMergePitch = kDim * 4 + 16;
 
+// The workspace status block (256 bytes): word 0 the status word; 64-bit words
+// kProbeWord.. accumulate the clock probe over calls (SM cycles, ns, calls).
+constexpr int kProbeWord = 1;
 // status codes written to the workspace status word on a timeout
 constexpr uint32_t kErrKLoad = 0x101, kErrVLoad = 0x102, kErrQK = 0x103, kErrPV = 0x104,
                    kErrSoftmax = 0x105, kErrDrain = 0x106;
@@ -101,6 +104,7 @@ struct Cfg;
 template <>
 struct Cfg<__nv_bfloat16> {
   static constexpr uint32_t kFmt = 1;
+  static constexpr uint32_t kPvFmt = 1;   // operand type of P.V (P and V)
   static constexpr uint32_t kRopeFmt = 1;
   static constexpr int kPParts = 2;
   static constexpr int kKStages = 4;
@@ -112,6 +116,7 @@ struct Cfg<__nv_bfloat16> {
 template <>
 struct Cfg<__half> {
   static constexpr uint32_t kFmt = 0;
+  static constexpr uint32_t kPvFmt = 0;
   static constexpr uint32_t kRopeFmt = 0;
   static constexpr int kPParts = 1;
   static constexpr int kKStages = 6;
@@ -133,19 +138,38 @@ struct Cfg<__half> {
 // type of q, q_pe, k_pe and out.
 template <typename T>
 struct Kv8 {};
+// The converter variant of a bf16 or fp16 call: V is not loaded by TMA but by
+// eight converter warps per CTA (warps 8..15) with 16-byte global loads of the
+// latent rows (L2 hits: the K producer read the same rows one tile earlier),
+// converted to fp16 in registers (exact for bf16 values within fp16's range;
+// a plain copy for fp16) and written once into the fp16 V operand stage.  P is
+// fp16 and P.V runs once (no bf16 hi/lo pair), and rows past a sequence's
+// length are written as zeros, so P.V never multiplies a zero weight by a
+// non-finite value the cache may hold there.
+template <typename T>
+struct Cv {};
 template <typename K>
 struct Io {
   using Out = K;
   static constexpr bool kKv8 = false;
+  static constexpr bool kConv = false;   // V through the converter warps
 };
 template <typename T>
 struct Io<Kv8<T>> {
   using Out = T;
   static constexpr bool kKv8 = true;
+  static constexpr bool kConv = false;
+};
+template <typename T>
+struct Io<Cv<T>> {
+  using Out = T;
+  static constexpr bool kKv8 = false;
+  static constexpr bool kConv = true;
 };
 template <typename T>
 struct Cfg<Kv8<T>> {
   static constexpr uint32_t kFmt = 0;
+  static constexpr uint32_t kPvFmt = 0;
   static constexpr uint32_t kRopeFmt = Cfg<T>::kFmt;
   static constexpr int kPParts = 1;
   static constexpr int kKStages = 8;                 // e4m3 latent or rope units as loaded
@@ -155,8 +179,20 @@ struct Cfg<Kv8<T>> {
   using PT = __half;
   static_assert(kV8Stages <= 8, "barrier arrays");
 };
+template <typename T>
+struct Cfg<Cv<T>> {
+  static constexpr uint32_t kFmt = Cfg<T>::kFmt;       // QK^T on the loaded K tiles
+  static constexpr uint32_t kPvFmt = 0;                // P.V in fp16
+  static constexpr uint32_t kRopeFmt = Cfg<T>::kFmt;
+  static constexpr int kPParts = 1;
+  static constexpr int kKStages = 4;
+  static constexpr uint32_t kKStageBytes = kStageBytes;
+  static constexpr int kVStages = 5;
+  static constexpr int kV8Stages = 0;
+  using PT = __half;
+};
 template <typename K>
-constexpr int threads_of() { return Io<K>::kKv8 ? 512 : 384; }
+constexpr int threads_of() { return (Io<K>::kKv8 || Io<K>::kConv) ? 512 : 384; }
 
 struct Barriers {
   uint64_t kfull[8], kempty[8];
@@ -199,6 +235,7 @@ struct Params {
   CUtensorMap tm_qpe;   // [qb][h][64]
   CUtensorMap tm_out;   // [qb][h][512] output rows, box 64 x 64 x 1 (stores; rows past h not written)
   CUtensorMap tm_part;  // [slots*128, 512] float32 partial rows, box 32 x 64 (stores)
+  const uint8_t* kv;    // raw latent rows (converter warps)
   const uint8_t* q;     // raw Q rows, for L2 prefetch
   const uint8_t* qpe;
   void* out;
@@ -787,7 +824,7 @@ __device__ __forceinline__ void pv_issuer(const Params& p, const Ctx& c, int pai
                                           uint32_t tmem, Barriers* bars) {
   using S = Smem<T>;
   constexpr int VS = Cfg<T>::kVStages;
-  constexpr uint32_t kIdesc = ptx::idesc_f16(Cfg<T>::kFmt, 128, 256, 1);
+  constexpr uint32_t kIdesc = ptx::idesc_f16(Cfg<T>::kPvFmt, 128, 256, 1);
   const uint32_t vfull0 = ptx::smem_u32(&bars->vfull[0]);
   const uint32_t vempty0 = ptx::smem_u32(&bars->vempty[0]);
   const uint32_t p_full0 = ptx::smem_u32(&bars->p_full[0]);
@@ -1508,6 +1545,10 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
   ptx::cluster_sync();
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  // clock probe: SM cycles and %globaltimer ns of this CTA's run (thread 0 of CTA 0)
+  const bool probe = blockIdx.x == 0 && threadIdx.x == 0 && p.status != nullptr;
+  const uint64_t probe_c0 = probe ? (uint64_t)clock64() : 0ull;
+  const uint64_t probe_t0 = probe ? ptx::globaltimer() : 0ull;
 
   Ctx c;
   c.abort_local = abort_flag;
@@ -1557,6 +1598,14 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
   ptx::tc_fence_before();
   __syncthreads();
   ptx::cluster_sync();
+  if (probe) {
+    // accumulated over calls in the workspace's status block (words 1..3 after the
+    // status word): cycles / ns is the SM clock the kernel actually ran at
+    unsigned long long* acc = reinterpret_cast<unsigned long long*>(p.status) + kProbeWord;
+    atomicAdd(acc, (unsigned long long)((uint64_t)clock64() - probe_c0));
+    atomicAdd(acc + 1, (unsigned long long)(ptx::globaltimer() - probe_t0));
+    atomicAdd(acc + 2, 1ull);
+  }
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc_pair(tmem, kTmemCols);

@@ -215,6 +215,13 @@ class MlaDecodeKernel:
             return 0
         return int(ws[:4].view(torch.int32).item())
 
+    def clock_probe(self, device, dtype) -> tuple:
+        """(SM cycles, ns, calls) the tensor-core kernel has accumulated in this
+        workspace: one CTA's run per call, timed by clock64 and %globaltimer, so
+        cycles / ns is the SM clock (GHz) while the kernel ran.  Reads the device
+        (synchronises the stream)."""
+        return _clock_probe(self._grouped._ws if self._grouped is not None else self._ws, device, dtype)
+
     def plan(self, dtype=torch.bfloat16) -> dict:
         """The library's plan for this shape: kernel, splits/pairs, launches per call."""
         self._one_kv_head("plan")
@@ -238,28 +245,60 @@ class MlaDecodeKernel:
                 f"cfg={self.cfg})")
 
 
-def combine(part_lse: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor, lse=None):
-    """LSE-merge ``num_split`` normalised partials (split-major) into ``out``.
+def _clock_probe(ws_map, device, dtype):
+    ws = ws_map.get((torch.device(device).index, dtype))
+    if ws is None or ws.numel() < 32:
+        return (0, 0, 0)
+    v = ws[8:32].view(torch.int64).tolist()
+    return (int(v[0]), int(v[1]), int(v[2]))
 
-    part_lse float32 [ns, b, h] (natural log), part_o float32 [ns, b, h, 512];
+
+def _split_major_view(name, t, inner_shape, device):
+    """Checks a [ns, *inner_shape] float32 view whose split dimension may have any
+    stride while each split is contiguous; returns the split stride in elements."""
+    if not isinstance(t, torch.Tensor) or t.device.type != "cuda" or t.dtype != torch.float32:
+        raise ValueError(f"{name} must be a float32 CUDA tensor")
+    if device is not None and t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    if tuple(t.shape[1:]) != tuple(inner_shape):
+        raise ValueError(f"{name} has shape {tuple(t.shape)}, expected (ns, {', '.join(map(str, inner_shape))})")
+    inner = 1
+    for d in range(t.dim() - 1, 0, -1):
+        if t.shape[d] != 1 and t.stride(d) != inner:
+            raise ValueError(f"{name}: every split must be contiguous")
+        inner *= t.shape[d]
+    return t.stride(0) if t.shape[0] > 1 else inner
+
+
+def combine(part_lse: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor, lse=None):
+    """LSE-merge ``num_split`` normalised partials into ``out``.
+
+    part_lse float32 [ns, b, h] (natural log), part_o float32 [ns, b, h, 512]:
+    split-major, or views whose split dimension has any stride (each split
+    contiguous, e.g. the per-GPU blocks of one packed all-gather buffer).
     ``out`` is float16, bfloat16 or float32 [b, h, 512].
     """
     ns, b, h = part_lse.shape
-    _check_tensor("part_lse", part_lse, (ns, b, h), torch.float32, None)
-    _check_tensor("part_o", part_o, (ns, b, h, DIM), torch.float32, part_lse.device)
+    dev = part_lse.device
+    lse_stride = _split_major_view("part_lse", part_lse, (b, h), None)
+    o_stride = _split_major_view("part_o", part_o, (b, h, DIM), dev)
     out_types = dict(_DTYPES)
     out_types[torch.float32] = capi.MLA_DTYPE_F32
     if out.dtype not in out_types:
         raise ValueError("out must be float16, bfloat16 or float32")
-    _check_tensor("out", out, (b, h, DIM), out.dtype, part_lse.device)
+    _check_tensor("out", out, (b, h, DIM), out.dtype, dev)
     lse_ptr = None
     if lse is not None:
-        _check_tensor("lse", lse, (b, h), torch.float32, part_lse.device)
+        _check_tensor("lse", lse, (b, h), torch.float32, dev)
         lse_ptr = lse.data_ptr()
-    with torch.cuda.device(part_lse.device):
-        stream = torch.cuda.current_stream(part_lse.device).cuda_stream
-    capi.combine(part_lse.data_ptr(), part_o.data_ptr(), ns, b, h, out.data_ptr(), lse_ptr,
-                 out_types[out.dtype], stream)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+    if part_lse.is_contiguous() and part_o.is_contiguous():
+        capi.combine(part_lse.data_ptr(), part_o.data_ptr(), ns, b, h, out.data_ptr(), lse_ptr,
+                     out_types[out.dtype], stream)
+    else:
+        capi.combine_strided(part_lse.data_ptr(), lse_stride, part_o.data_ptr(), o_stride, ns, b, h,
+                             out.data_ptr(), lse_ptr, out_types[out.dtype], stream)
 
 
 class MlaPagedDecodeKernel:
@@ -311,6 +350,11 @@ class MlaPagedDecodeKernel:
                     ws = torch.zeros(self.workspace_bytes(dtype), dtype=torch.uint8, device=device)
                     self._ws[key] = ws
         return ws
+
+    def clock_probe(self, device, dtype) -> tuple:
+        """(SM cycles, ns, calls) of the decode kernel accumulated in this workspace
+        (see ``MlaDecodeKernel.clock_probe``)."""
+        return _clock_probe(self._ws, device, dtype)
 
     def device_status(self, device, dtype) -> int:
         """Status word the kernel leaves in the workspace (0 = no timeout)."""

@@ -69,7 +69,10 @@ class SequenceSplitDecoder:
 
     ``partial_fn(q, q_pe, kv, k_pe, o, lse)`` and ``combine_fn(part_lse,
     part_o, out, lse)`` default to the CUDA kernels; tests on CPU ranks pass
-    their own.
+    their own.  Every rank's (O, LSE) lives in one packed block of a
+    [world, b*h*513 + padding] float32 buffer, so a call issues a single
+    all-gather (in place) and the merge reads the gathered blocks where they
+    landed (``combine`` with a split stride).
     """
 
     def __init__(self, batch: int, heads: int, seqlen_kv: int, group=None, cfg=None,
@@ -88,16 +91,20 @@ class SequenceSplitDecoder:
         self._combine = combine_fn or combine
         self._bufs = {}
 
+    def _chunk(self) -> int:
+        """Floats per rank in the gather buffer: O (b*h*512), LSE (b*h), padded to 256 bytes."""
+        bh = self.batch * self.heads
+        return bh * DIM + -(-bh // 64) * 64
+
     def _buffers(self, device):
+        """The packed gather buffer [world, chunk] and this rank's (O, LSE) views of its own block."""
         key = (device.type, device.index)
         if key not in self._bufs:
             b, h, w = self.batch, self.heads, self.world
-            self._bufs[key] = (
-                torch.empty(b, h, DIM, dtype=torch.float32, device=device),
-                torch.empty(b, h, dtype=torch.float32, device=device),
-                torch.empty(w, b, h, DIM, dtype=torch.float32, device=device),
-                torch.empty(w, b, h, dtype=torch.float32, device=device),
-            )
+            buf = torch.empty(w, self._chunk(), dtype=torch.float32, device=device)
+            mine = buf[self.rank]
+            self._bufs[key] = (buf, mine[: b * h * DIM].view(b, h, DIM),
+                               mine[b * h * DIM: b * h * (DIM + 1)].view(b, h))
         return self._bufs[key]
 
     def __call__(self, q, q_pe, kv_part, k_pe_part, out, lse=None):
@@ -105,14 +112,15 @@ class SequenceSplitDecoder:
         self.merge(out, lse, q.device)
 
     def local(self, q, q_pe, kv_part, k_pe_part):
-        """This rank's part: normalised float32 O and LSE of its KV rows."""
+        """This rank's part: normalised float32 O and LSE of its KV rows, written
+        straight into its block of the gather buffer."""
         b, h = self.batch, self.heads
         if tuple(q.shape) != (b, h, DIM):
             raise ValueError(f"q has shape {tuple(q.shape)}, expected {(b, h, DIM)}")
         if kv_part.shape[1] != self.local_len or k_pe_part.shape[1] != self.local_len:
             raise ValueError(f"rank {self.rank} holds KV rows [{self.start}, {self.end}): "
                              f"expected {self.local_len} rows, got {kv_part.shape[1]}")
-        o, l, _, _ = self._buffers(q.device)
+        _, o, l = self._buffers(q.device)
         if self.local_len > 0:
             self._partial(q, q_pe, kv_part, k_pe_part, o, l)
         else:
@@ -121,10 +129,12 @@ class SequenceSplitDecoder:
             l.fill_(float("-inf"))
 
     def merge(self, out, lse=None, device=None):
-        """All-gather every rank's part over the process group and LSE-merge it into ``out``."""
+        """One all-gather of every rank's packed (O, LSE) block over the process group
+        (in place: this rank's block is the input), then the LSE merge into ``out``."""
         b, h, w = self.batch, self.heads, self.world
-        o, l, o_all, l_all = self._buffers(device if device is not None else out.device)
-        # gathered along dim 0: [world * batch, ...] is the [world, batch, ...] stack
-        dist.all_gather_into_tensor(o_all.view(w * b, h, DIM), o, group=self.group)
-        dist.all_gather_into_tensor(l_all.view(w * b, h), l, group=self.group)
+        buf, _, _ = self._buffers(device if device is not None else out.device)
+        dist.all_gather_into_tensor(buf.view(-1), buf[self.rank], group=self.group)
+        bh = b * h
+        o_all = buf[:, : bh * DIM].view(w, b, h, DIM)
+        l_all = buf[:, bh * DIM: bh * (DIM + 1)].view(w, b, h)
         self._combine(l_all, o_all, out, lse)

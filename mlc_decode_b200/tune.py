@@ -4,7 +4,7 @@ The role of the reference's ``scripts/tune_best.py`` (and its frozen
 ``mla_best_configs.json``): time candidate configs per shape and keep the
 fastest, keyed by shape, dtype and GPU count as ``plan.lookup`` reads it.
 
-    python -m mlc_decode_b200.tune                  # the BASELINE shapes
+    python -m mlc_decode_b200.tune                  # the benchmark shapes
     python -m mlc_decode_b200.tune --shape 64,128,8192,bf16 --out table.json
 
 Candidates are the library default and CTA-pair counts around the SM count
@@ -27,10 +27,10 @@ import torch
 from . import plan
 from .decode import MlaDecodeKernel
 
-# (batch, heads, kv_ctx, dtype) per GPU for BASELINE.json's configs: C1, C2, C3
+# (batch, heads, kv_ctx, dtype) per GPU of the benchmark configs: C1, C2, C3
 # (ns sweep shape), the C4 head sweep, C5a per GPU at 1/2/4/8 GPUs, C5b per GPU
 # at 1/2/4/8 GPUs (sequence split: each GPU holds kv_ctx / N rows).
-BASELINE_SHAPES = [
+BENCH_SHAPES = [
     (2, 16, 1024, "fp16"), (64, 128, 8192, "bf16"), (132, 128, 16384, "fp16"),
     (128, 16, 4096, "bf16"), (128, 32, 4096, "bf16"), (128, 64, 4096, "bf16"), (128, 128, 4096, "bf16"),
     (512, 128, 4096, "bf16"), (256, 128, 4096, "bf16"), (64, 128, 4096, "bf16"),
@@ -110,7 +110,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1, help="GPU count the entries are keyed for")
     ap.add_argument("--out", default=plan.TABLE_PATH)
     a = ap.parse_args()
-    shapes = BASELINE_SHAPES
+    shapes = BENCH_SHAPES
     if a.shape:
         shapes = []
         for s in a.shape:

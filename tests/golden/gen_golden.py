@@ -42,7 +42,7 @@ from oracle.mla_oracle import make_inputs, make_inputs_ext  # noqa: E402
 
 # (name, dtype, batch, heads, kv_ctx, seed, scale)
 CASES = [
-    ("c1_fp16_b2_h16_s1024", "fp16", 2, 16, 1024, 0, 1.0),
+    ("c1_fp16_b2_h16_s1024", "fp16", 2, 16, 1024, 0, 1.0),       # the CPU-runnable reference case
     ("c1_fp16_b2_h16_s1024_x0.1", "fp16", 2, 16, 1024, 0, 0.1),  # check_mla.py distribution
     ("tail_fp16_s7", "fp16", 1, 16, 7, 1, 1.0),
     ("tail_fp16_s33", "fp16", 1, 16, 33, 2, 1.0),
@@ -55,6 +55,8 @@ CASES = [
     ("h64_bf16_s513", "bf16", 1, 64, 513, 9, 1.0),
     ("h128_bf16_s640", "bf16", 2, 128, 640, 10, 1.0),
     ("h128_fp16_s1000_x0.1", "fp16", 1, 128, 1000, 11, 0.1),
+    ("bench_bf16_b1_h128_s8192", "bf16", 1, 128, 8192, 12, 1.0),   # one sequence of the bench call
+    ("longcache_fp16_b1_h128_s16384", "fp16", 1, 128, 16384, 13, 1.0),
 ]
 
 # (name, dtype, batch, heads, kv_heads, kv_ctx, seed): grouped KV heads
@@ -121,8 +123,10 @@ def main():
         arrays[f"{name}/out64"] = out64.float().numpy()  # float32 storage of the float64 result
         arrays[f"{name}/out_native"] = outn.float().numpy()
         arrays[f"{name}/lse64"] = lse.numpy()
+        # the native-dtype output of a long sequence depends on torch's CPU thread
+        # count (reduction order): record it so a test can replay it exactly
         meta.append({"name": name, "dtype": dtype, "batch": b, "heads": h, "kv_ctx": s,
-                     "seed": seed, "scale": scale,
+                     "seed": seed, "scale": scale, "threads": torch.get_num_threads(),
                      "sha256": [digest(t) for t in (q, q_pe, kv, k_pe)]})
     np.savez_compressed(os.path.join(HERE, "ref_program.npz"), **arrays)
     with open(os.path.join(HERE, "ref_program_cases.json"), "w") as f:

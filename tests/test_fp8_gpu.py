@@ -39,7 +39,7 @@ def _run(b, h, s, dtype, seed, scale, x=1.0, cfg=None, calls=1):
 @pytest.mark.parametrize("b,h,s,dtype,scale", [
     (64, 128, 2048, "bf16", 1 / 16),   # whole sequences per CTA pair
     (4, 128, 1000, "bf16", 1 / 16),    # split sequences, merged in the kernel
-    (2, 16, 1024, "fp16", 1 / 32),     # BASELINE configs[0] shape, many pieces: combine launch
+    (2, 16, 1024, "fp16", 1 / 32),     # the CPU-runnable reference shape, many pieces: combine launch
     (3, 64, 777, "bf16", 0.05),        # rows past h, ragged tail tile, non-power-of-two scale
     (2, 200, 513, "fp16", 1.0),        # two head groups
 ])

@@ -116,7 +116,7 @@ def test_large_scores_stress_the_max_path(qscale, cuda):
 
 
 def test_kernels_agree_at_c2_size_on_sampled_batches(cuda):
-    """BASELINE configs[1] shape (b64 h128 s8192 bf16): the default path vs the
+    """The DeepSeek-V3-shaped bench case (b64 h128 s8192 bf16): the default path vs the
     CUDA-core path on the full batch, and both vs the oracle on sampled sequences."""
     from mlc_decode_b200 import MlaDecodeKernel
 
