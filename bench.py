@@ -76,6 +76,8 @@ def parse_args():
     ap.add_argument("--dtype", choices=["bf16", "fp16"], default="bf16")
     ap.add_argument("--kernel", choices=["auto", "tc", "simt"], default="auto")
     ap.add_argument("--num-split", type=int, default=0)
+    ap.add_argument("--combine-groups", type=int, default=0,
+                    help="config key combine_groups (>= 2: wide splits merged by a separate combine launch)")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="budget of host-core time for the cpu_baseline sample")
@@ -304,6 +306,8 @@ def run_ours(a, rank, world, local_rank):
     cfg = {"kernel": a.kernel}
     if a.num_split:
         cfg["num_split"] = a.num_split
+    if a.combine_groups:
+        cfg["combine_groups"] = a.combine_groups
 
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     q = torch.randn(b, h, 512, device=dev, generator=g).to(tdt)

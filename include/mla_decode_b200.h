@@ -56,8 +56,13 @@ enum MlaKernelKind {
  * (mla_decode.py:588-598, 720-729): block_N KV rows per tile, block_H heads
  * per CTA, num_split requested KV splits per sequence, spread selects the
  * whole-wave split family of _split_plan (mla_decode.py:9-30), num_stages the
- * depth of the shared-memory pipeline.  combine_groups is accepted and
- * ignored (the combine kernel is single pass).  softmax_scale is the factory
+ * depth of the shared-memory pipeline.  A sequence the tensor-core kernel
+ * splits between more than 3 CTA pairs is merged by a separate combine launch
+ * (single pass for any combine_groups >= 0: the reference's second stage,
+ * mla_decode.py:248-259, is not needed); combine_groups < 0 (an extension: the
+ * reference never passes it) asks for that merge inside the decode launch
+ * instead, by all of the sequence's CTA pairs in a cooperative launch.
+ * softmax_scale is the factory
  * argument of the same name (mla_decode.py:38).  Zero fields mean "choose".
  */
 typedef struct MlaCfg {
@@ -100,8 +105,10 @@ size_t mla_workspace_bytes(int32_t batch, int32_t heads, int32_t seqlen_kv,
  *   out4[0] kernel (enum MlaKernelKind, never AUTO)
  *   out4[1] KV splits per sequence (CUDA-core kernel) or CTA pairs (tensor-core kernel)
  *   out4[2] kernel launches per call (1 or 2; the tensor-core kernel merges a
- *           sequence split between a few CTA pairs itself, and leaves sequences
- *           split between many pairs to a combine launch)
+ *           sequence split between at most 3 CTA pairs itself, by the last of
+ *           them; one split between more goes to a combine launch, unless
+ *           cfg->combine_groups < 0 asks all of its pairs to merge it inside the
+ *           kernel in a cooperative launch)
  *   out4[3] bytes at the start of the workspace that must be zero before the
  *           first call with it (the tensor-core kernel's status word and piece
  *           counters; every call leaves them zero again)

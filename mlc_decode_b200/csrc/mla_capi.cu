@@ -103,7 +103,7 @@ int resolve(int batch, int heads, int seqlen_kv, const MlaCfg* cfg, Resolved* r)
 }
 
 // Workspace layout:
-//   tensor-core kernel: [status word, 256 B][piece counters uint32 x batch x ceil(heads/128) x 2,
+//   tensor-core kernel: [status word, 256 B][piece counters uint32 x batch x ceil(heads/128) x 4,
 //                       padded to 256 B]
 //                       [partial LSE float32 x rows, padded to 256 B][partial O float32 x rows x 512]
 //                       (partials only when some sequence is split between CTA pairs)
@@ -114,9 +114,10 @@ int resolve(int batch, int heads, int seqlen_kv, const MlaCfg* cfg, Resolved* r)
 // at bytes 8, 16, 24, accumulated over calls).
 constexpr size_t kStatusBytes = 256;
 
-// one counter per (sequence, group of 128 heads, CTA rank) of the tensor-core kernel
+// four counters per (sequence, group of 128 heads) of the tensor-core kernel: pieces
+// published and CTAs done merging, per CTA rank
 size_t counter_bytes(int batch, int heads) {
-  return align_up((size_t)batch * head_groups(heads) * 2 * sizeof(uint32_t), 256);
+  return align_up((size_t)batch * head_groups(heads) * 4 * sizeof(uint32_t), 256);
 }
 
 size_t part_rows(int batch, int heads, const Resolved& r) {
@@ -168,7 +169,7 @@ int32_t mla_describe_plan(int32_t batch, int32_t heads, int32_t seqlen_kv, int32
   const bool tc = r.kernel == MLA_KERNEL_TC;
   out4[0] = r.kernel;
   out4[1] = tc ? r.plan.bpc : r.plan.ns;
-  out4[2] = (r.plan.needs_combine && (!tc || r.tc_variant == 1)) ? 2 : 1;
+  out4[2] = (r.plan.needs_combine && (!tc || r.tc_variant == 1)) ? 2 : 1;   // (variant 2: merged in-kernel)
   out4[3] = tc ? (int64_t)(kStatusBytes + counter_bytes(batch, heads)) : 0;
   return MLA_OK;
 }
@@ -285,8 +286,9 @@ int run_splitkv(const char* fn, const DecodeArgs& a, const Resolved& r) {
 
 int run_combine_ws(const char* fn, const DecodeArgs& a, const Resolved& r) {
   // the decode kernel wrote out/lse itself: single-split plans, and tensor-core
-  // plans whose sequences are split between a few CTA pairs (merged in-kernel)
-  if (!r.plan.needs_combine || (r.kernel == MLA_KERNEL_TC && r.tc_variant == 0)) return MLA_OK;
+  // plans whose split sequences it merged (variant 0: split between a few CTA
+  // pairs; variant 2: merged by all their pairs in a cooperative launch)
+  if (!r.plan.needs_combine || (r.kernel == MLA_KERNEL_TC && r.tc_variant != 1)) return MLA_OK;
   const cudaError_t err =
       r.kernel == MLA_KERNEL_TC
           ? launch_sm100_combine(a)
@@ -481,7 +483,7 @@ int32_t mla_selftest_wait_timeout(uint32_t* status, uint64_t* result, uint64_t l
 
 // ---------------------------------------------------------------------------
 // Ragged / paged decode (per-sequence KV lengths, optional page table).
-// Workspace: [status 256 B][counters u32 x batch x groups x 2, padded][tile prefix
+// Workspace: [status 256 B][counters u32 x batch x groups x 4, padded][tile prefix
 // sums u32 x (batch x groups + 1), padded][partial LSE][partial O].
 // ---------------------------------------------------------------------------
 namespace mla {
@@ -617,9 +619,12 @@ int decode_ext(const char* fn, const void* q, const void* q_pe, const void* kv_c
   a.page_size = block_table != nullptr ? page_size : 0;
   a.num_pages = block_table != nullptr ? num_pages : 0;
   a.max_pages = block_table != nullptr ? max_pages_per_seq : 0;
-  cudaError_t err = launch_sm100_ragged_plan(a);   // lengths clamped as the decode kernel does
-  if (err == cudaSuccess) err = launch_sm100_decode(a, 1);
-  if (err == cudaSuccess) err = launch_sm100_combine(a);
+  // lengths clamped as the decode kernel does; sequences split between many pairs
+  // merged in the kernel (cooperative launch) or by the combine launch
+  const int variant = (sm100_coop_available() && cfg != nullptr && cfg->combine_groups < 0) ? 2 : 1;
+  cudaError_t err = launch_sm100_ragged_plan(a);
+  if (err == cudaSuccess) err = launch_sm100_decode(a, variant);
+  if (err == cudaSuccess && variant == 1) err = launch_sm100_combine(a);
   if (err != cudaSuccess) {
     set_error("%s: launch failed: %s", fn, cudaGetErrorString(err));
     return MLA_ERR_CUDA;

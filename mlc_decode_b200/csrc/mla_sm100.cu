@@ -84,7 +84,14 @@ constexpr float kRescaleLog2 = 8.0f;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr int kMaxPairs = 256;        // CTA pairs per launch (schedule bound)
 constexpr int kFuseMaxPieces = 3;     // most pieces of one sequence merged in-kernel
+// bf16 calls run the Cv variant (each V stage converted to fp16 in place by the
+// converter warps: one P.V pass, fp16 P); fp16 calls the plain variant (V is
+// already fp16; only tail units are rewritten)
+constexpr bool kConvV = true;
 constexpr double kWholeSlack = 10.0;  // tiles per pair a whole-sequence assignment may add
+// The cooperative merge stages up to 128 KB + 16 bytes a piece from offset 0 and
+// keeps its tables at this offset (all below the barrier block of every variant).
+constexpr uint32_t kMergeTab = 136 * 1024;
 // A merge stages another pair's 64 partial rows (fp32, 2 KB each) in shared memory
 // at this row pitch (16 bytes of padding: threads reading one column of 32 rows
 // hit distinct banks).
@@ -95,7 +102,7 @@ constexpr uint32_t kMergePitch = kDim * 4 + 16;
 constexpr int kProbeWord = 1;
 // status codes written to the workspace status word on a timeout
 constexpr uint32_t kErrKLoad = 0x101, kErrVLoad = 0x102, kErrQK = 0x103, kErrPV = 0x104,
-                   kErrSoftmax = 0x105, kErrDrain = 0x106;
+                   kErrSoftmax = 0x105, kErrDrain = 0x106, kErrMerge = 0x107;
 
 // Compile-time configuration per input type.  bf16 needs the hi/lo P pair
 // (two P operands); fp16 P is exact enough and gives the space to the rings.
@@ -138,15 +145,15 @@ struct Cfg<__half> {
 // type of q, q_pe, k_pe and out.
 template <typename T>
 struct Kv8 {};
-// The converter variant of a bf16 or fp16 call: V is not loaded by TMA but by
-// eight converter warps per CTA (warps 8..15) with 16-byte global loads of the
-// latent rows (L2 hits: the K producer read the same rows one tile earlier),
-// converted to fp16 in registers (exact for bf16 values within fp16's range;
-// a plain copy for fp16) and written once into the fp16 V operand stage.  P is
-// fp16 and P.V runs once (no bf16 hi/lo pair), and rows past a sequence's
-// length are written as zeros, so P.V never multiplies a zero weight by a
-// non-finite value the cache may hold there.
-template <typename T>
+// The converter variant of a bf16 or fp16 call: each CTA's V producer loads V by
+// TMA into its own stage of the V ring (a local barrier), and four converter
+// warps (warps 12..15) rewrite the landed stage in place before the P.V issuer
+// may read it: rows past the sequence's length become zeros (P.V then never
+// multiplies a zero weight by a non-finite value the cache may hold there:
+// uninitialised or recycled pages, another sequence's rows) and, with kF16 (bf16
+// inputs), every value is converted to fp16 (exact within fp16's range), so P is
+// fp16 and P.V runs once instead of as the bf16 hi/lo pair.
+template <typename T, bool kF16>
 struct Cv {};
 template <typename K>
 struct Io {
@@ -160,8 +167,8 @@ struct Io<Kv8<T>> {
   static constexpr bool kKv8 = true;
   static constexpr bool kConv = false;
 };
-template <typename T>
-struct Io<Cv<T>> {
+template <typename T, bool kF16>
+struct Io<Cv<T, kF16>> {
   using Out = T;
   static constexpr bool kKv8 = false;
   static constexpr bool kConv = true;
@@ -179,17 +186,19 @@ struct Cfg<Kv8<T>> {
   using PT = __half;
   static_assert(kV8Stages <= 8, "barrier arrays");
 };
-template <typename T>
-struct Cfg<Cv<T>> {
+template <typename T, bool kF16>
+struct Cfg<Cv<T, kF16>> {
+  // converting bf16 V to fp16: fp16 P, one P.V pass, the P space goes to the V ring
+  static constexpr bool kToF16 = kF16 && std::is_same<T, __nv_bfloat16>::value;
   static constexpr uint32_t kFmt = Cfg<T>::kFmt;       // QK^T on the loaded K tiles
-  static constexpr uint32_t kPvFmt = 0;                // P.V in fp16
+  static constexpr uint32_t kPvFmt = kToF16 ? 0u : Cfg<T>::kPvFmt;
   static constexpr uint32_t kRopeFmt = Cfg<T>::kFmt;
-  static constexpr int kPParts = 1;
-  static constexpr int kKStages = 4;
+  static constexpr int kPParts = kToF16 ? 1 : Cfg<T>::kPParts;
+  static constexpr int kKStages = Cfg<T>::kKStages;
   static constexpr uint32_t kKStageBytes = kStageBytes;
-  static constexpr int kVStages = 5;
+  static constexpr int kVStages = kToF16 ? 5 : Cfg<T>::kVStages;
   static constexpr int kV8Stages = 0;
-  using PT = __half;
+  using PT = typename std::conditional<kToF16, __half, typename Cfg<T>::PT>::type;
 };
 template <typename K>
 constexpr int threads_of() { return (Io<K>::kKv8 || Io<K>::kConv) ? 512 : 384; }
@@ -197,7 +206,8 @@ constexpr int threads_of() { return (Io<K>::kKv8 || Io<K>::kConv) ? 512 : 384; }
 struct Barriers {
   uint64_t kfull[8], kempty[8];
   uint64_t vfull[8], vempty[8];
-  uint64_t v8full[8], v8empty[8];   // FP8 variant: e4m3 V units as loaded
+  uint64_t v8full[8], v8empty[8];   // FP8 variant: e4m3 V units as loaded (plain and Cv: local V landing)
+  uint64_t vfix[8];                 // plain variants: a tail unit rewritten in both CTAs
   uint64_t q_full, q_empty, qt_full;
   uint64_t s_full[2], s_free[2];
   uint64_t p_full[2];
@@ -226,6 +236,7 @@ struct Smem {
   static constexpr uint32_t kMisc = kXl + 128 * 4;
   static constexpr uint32_t kBytes = kMisc + 64 + 1024;   // + alignment slack
   static_assert(kBytes <= 232448, "shared memory");
+  static_assert(kBar >= kMergeTab + 6 * 1024, "cooperative merge staging");
 };
 
 struct Params {
@@ -243,7 +254,8 @@ struct Params {
   float* part_o;
   float* part_lse;
   uint32_t* status;
-  uint32_t* counters;   // [batch][2] pieces finished per (sequence, CTA rank); zero between calls
+  uint32_t* counters;   // [batch][4] per sequence: pieces published per CTA rank, then (cooperative
+                        // merges) CTAs done merging per rank; zero between calls
   float kv_scale;       // FP8 variant: dequantisation scale of the e4m3 latent rows
   // Work units are "virtual sequences".  The query side is qb = b x q_len x
   // kv_heads query sequences qs = (s * q_len + t) * kv_heads + kvh (query
@@ -258,6 +270,7 @@ struct Params {
   int q_len, kv_heads;  // query positions per sequence, KV heads
   int out_f32;          // `out` is float32 (tm_out then has 32 x 64 float boxes)
   int fuse_max;         // sequences split into at most this many pieces are merged here
+  int coop;             // cooperative launch: wider splits are merged here too (every pair waits)
   // Ragged calls (per-sequence lengths, optionally paged KV): cu_tiles[v] is the
   // first tile of virtual sequence v in the flattened list (batch + 1 entries,
   // written by the plan kernel); nullptr for fixed-length calls.
@@ -632,7 +645,33 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
         }
       }
     }
+  } else if constexpr (Io<T>::kConv) {
+    // Cv: this CTA's 128 latent columns of the tile's 64-token halves into its own
+    // stage, landing on a local barrier: the converter warps rewrite the stage
+    // before the P.V issuer is told it is full
+    const uint32_t land0 = ptx::smem_u32(&bars->v8full[0]);
+    while (it.next(&pc)) {
+      const int vseq = vseq_kvseq(p, pc.bb), kvh = vseq_kvh(p, pc.bb), vlen = seq_len(p, pc.bb);
+#pragma unroll 1
+      for (int j = pc.first; j < pc.end; ++j) {
+        const int yv0 = kv_row(p, vseq, j * kTile, vlen), yv1 = kv_row(p, vseq, j * kTile + 64, vlen);
+#pragma unroll 1
+        for (int u = 0; u < 4; ++u) {
+          const int nh = u >> 1, th = u & 1;
+          if (!wait_bar(c, vempty0 + 8 * ring.stage, ring.phase ^ 1u, kErrVLoad)) return;
+          const uint32_t bar = land0 + 8 * ring.stage;
+          ptx::mbar_arrive_expect_tx(bar, kStageBytes);
+          const uint32_t dst = sbase + S::kVRing + ring.stage * kStageBytes;
+          const int x = 256 * nh + 128 * (int)rank;
+          const int yv = th == 0 ? yv0 : yv1;
+          ptx::tma_load_3d_local_hint(dst, &p.tm_kv, bar, x, kvh, yv, once);
+          ptx::tma_load_3d_local_hint(dst + kChunkBytes, &p.tm_kv, bar, x + 64, kvh, yv, once);
+          ring.advance();
+        }
+      }
+    }
   } else {
+  const uint32_t land0 = ptx::smem_u32(&bars->v8full[0]);
   while (it.next(&pc)) {
     const int vseq = vseq_kvseq(p, pc.bb), kvh = vseq_kvh(p, pc.bb), vlen = seq_len(p, pc.bb);
 #pragma unroll 1
@@ -643,14 +682,23 @@ __device__ __forceinline__ void v_producer(const Params& p, const Ctx& c, uint32
       for (int u = 0; u < 4; ++u) {
         const int nh = u >> 1, th = u & 1;
         if (!wait_bar(c, vempty0 + 8 * ring.stage, ring.phase ^ 1u, kErrVLoad)) return;
-        if (leader) ptx::mbar_arrive_expect_tx(vfull0 + 8 * ring.stage, 2 * kStageBytes);
         const uint32_t dst = sbase + S::kVRing + ring.stage * kStageBytes;
-        const uint32_t bar = vfull0_leader + 8 * ring.stage;
         const int x = 256 * nh + 128 * (int)rank;
         // the latent rows' last read
         const int yv = th == 0 ? yv0 : yv1;
-        ptx::tma_load_3d_pair_hint(dst, &p.tm_kv, bar, x, kvh, yv, once);
-        ptx::tma_load_3d_pair_hint(dst + kChunkBytes, &p.tm_kv, bar, x + 64, kvh, yv, once);
+        if (vlen - (j * kTile + 64 * th) < 64) {
+          // a tail unit: into this CTA's stage on a local barrier; the tail fixer zeroes
+          // the rows past the length before the stage is reported full
+          const uint32_t bar = land0 + 8 * ring.stage;
+          ptx::mbar_arrive_expect_tx(bar, kStageBytes);
+          ptx::tma_load_3d_local_hint(dst, &p.tm_kv, bar, x, kvh, yv, once);
+          ptx::tma_load_3d_local_hint(dst + kChunkBytes, &p.tm_kv, bar, x + 64, kvh, yv, once);
+        } else {
+          if (leader) ptx::mbar_arrive_expect_tx(vfull0 + 8 * ring.stage, 2 * kStageBytes);
+          const uint32_t bar = vfull0_leader + 8 * ring.stage;
+          ptx::tma_load_3d_pair_hint(dst, &p.tm_kv, bar, x, kvh, yv, once);
+          ptx::tma_load_3d_pair_hint(dst + kChunkBytes, &p.tm_kv, bar, x + 64, kvh, yv, once);
+        }
         ring.advance();
       }
     }
@@ -689,6 +737,7 @@ __device__ __forceinline__ void v_converter(const Params& p, const Ctx& c, int p
   PieceIter it(p, pair);
   Piece pc;
   while (it.next(&pc)) {
+    const int klen = seq_len(p, pc.bb);
 #pragma unroll 1
     for (int j = pc.first; j < pc.end; ++j) {
 #pragma unroll 1
@@ -697,13 +746,16 @@ __device__ __forceinline__ void v_converter(const Params& p, const Ctx& c, int p
         if (!wait_bar(c, op_empty + 8 * rop.stage, rop.phase ^ 1u, kErrVLoad)) return;
         const uint8_t* src = ring8 + r8.stage * kChunkBytes;
         uint8_t* dst = ring_op + rop.stage * kStageBytes;
+        // rows past the sequence's length become zeros (whatever codes the cache holds there)
+        const int nvalid = klen - (j * kTile + 64 * (u & 1));
         // all of this thread's granules in flight before any conversion
         uint4 x[kPer];
 #pragma unroll
         for (int k = 0; k < kPer; ++k) {
           // logical 16-byte granule g of row r (elements [16 g, 16 g + 16)) sits at g ^ (r & 7)
           const int i = ct + 32 * kConvWarps * k, r = i >> 3, g = i & 7;
-          x[k] = *reinterpret_cast<const uint4*>(src + r * 128 + ((g ^ (r & 7)) << 4));
+          x[k] = r < nvalid ? *reinterpret_cast<const uint4*>(src + r * 128 + ((g ^ (r & 7)) << 4))
+                            : make_uint4(0u, 0u, 0u, 0u);
         }
 #pragma unroll
         for (int k = 0; k < kPer; ++k) {
@@ -726,6 +778,130 @@ __device__ __forceinline__ void v_converter(const Params& p, const Ctx& c, int p
         }
         r8.advance();
         rop.advance();
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Tail fixer of the plain variants (warp 9 of each CTA).  A V unit whose 64 token
+// rows run past the sequence's length (the last tile of a sequence) is loaded by
+// the V producer into this CTA's stage on a local barrier instead of the pair
+// barrier; this warp zeroes the rows past the length (so that P = 0 never meets a
+// non-finite value the cache holds there: uninitialised or recycled pages,
+// another sequence's rows), signals the even CTA's fixer, which reports the stage
+// full to the P.V issuer once both halves are done.  Full units are not touched.
+// Tail units are rare, so each stage's local barriers keep their own phase bit.
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void v_tailfix(const Params& p, const Ctx& c, uint32_t rank, int pair, uint8_t* smem,
+                                          Barriers* bars, int lane) {
+  using S = Smem<T>;
+  constexpr int VS = Cfg<T>::kVStages;
+  const uint32_t land0 = ptx::smem_u32(&bars->v8full[0]);
+  const uint32_t fix0 = ptx::smem_u32(&bars->vfix[0]);
+  const uint32_t fix0_leader = ptx::mapa(fix0, 0);
+  const uint32_t vfull0 = ptx::smem_u32(&bars->vfull[0]);
+  uint8_t* ring = smem + S::kVRing;
+  uint32_t par = 0;   // per stage: phase of its next tail use
+  Ring<VS> rg;
+  PieceIter it(p, pair);
+  Piece pc;
+  while (it.next(&pc)) {
+    const int vlen = seq_len(p, pc.bb);
+#pragma unroll 1
+    for (int j = pc.first; j < pc.end; ++j) {
+#pragma unroll 1
+      for (int u = 0; u < 4; ++u) {
+        const int nvalid = vlen - (j * kTile + 64 * (u & 1));
+        if (nvalid < 64) {
+          const uint32_t ph = (par >> rg.stage) & 1u;
+          if (!wait_bar(c, land0 + 8 * rg.stage, ph, kErrVLoad)) return;
+          uint4* st = reinterpret_cast<uint4*>(ring + rg.stage * kStageBytes);
+          // 1024 16-byte granules; granule i is in row (i / 8) % 64 whatever the swizzle
+#pragma unroll 4
+          for (int i = lane; i < 1024; i += 32)
+            if (((i >> 3) & 63) >= nvalid) st[i] = make_uint4(0u, 0u, 0u, 0u);
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            ptx::mbar_arrive_cluster(fix0_leader + 8 * rg.stage);
+            if (rank == 0) {
+              // both CTAs' halves are rewritten: the stage is full for the P.V issuer
+              if (!wait_bar(c, fix0 + 8 * rg.stage, ph, kErrVLoad)) return;
+              ptx::mbar_arrive_local(vfull0 + 8 * rg.stage);
+            }
+          }
+          __syncwarp();
+          par ^= 1u << rg.stage;
+        }
+        rg.advance();
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Converter warps of the Cv variant (warps 12..15): every V unit of the ring, as
+// the V producer's local TMA lands it (this CTA's 128 latent dims of 64 tokens,
+// two SW128 boxes), is rewritten in place: rows past the sequence's length as
+// zeros, and (kToF16) bf16 values as fp16.  The conversion is elementwise, so the
+// swizzle does not matter: thread ct takes 16-byte granules ct + 128 k of the
+// 16 KB stage (row = (granule / 8) % 64).  Then each warp signals the stage to
+// the even CTA's P.V issuer (count 4 warps x 2 CTAs).
+// ---------------------------------------------------------------------------
+constexpr int kFixWarps = 4;
+
+// two bf16 (low half first) -> two fp16, round to nearest (exact in fp16's range)
+__device__ __forceinline__ uint32_t bf16x2_to_h2(uint32_t w) {
+  return Elt<__half>::pack2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+template <typename KT>
+__device__ __forceinline__ void v_fix(const Params& p, const Ctx& c, int pair, uint8_t* smem, Barriers* bars,
+                                      int ct, int lane) {
+  using S = Smem<KT>;
+  constexpr int VS = Cfg<KT>::kVStages;
+  constexpr bool kToF16 = Cfg<KT>::kToF16;
+  constexpr int kPer = (int)kStageBytes / 16 / (32 * kFixWarps);   // granules per thread and unit
+  const uint32_t land0 = ptx::smem_u32(&bars->v8full[0]);
+  const uint32_t full0_leader = ptx::mapa(ptx::smem_u32(&bars->vfull[0]), 0);
+  uint8_t* ring = smem + S::kVRing;
+  Ring<VS> rg;
+  PieceIter it(p, pair);
+  Piece pc;
+  while (it.next(&pc)) {
+    const int klen = seq_len(p, pc.bb);
+#pragma unroll 1
+    for (int j = pc.first; j < pc.end; ++j) {
+#pragma unroll 1
+      for (int u = 0; u < 4; ++u) {
+        if (!wait_bar(c, land0 + 8 * rg.stage, rg.phase, kErrVLoad)) return;
+        uint4* st = reinterpret_cast<uint4*>(ring + rg.stage * kStageBytes);
+        const int nvalid = klen - (j * kTile + 64 * (u & 1));
+        if constexpr (kToF16) {
+          uint4 x[kPer];
+#pragma unroll
+          for (int k = 0; k < kPer; ++k) x[k] = st[ct + 128 * k];
+#pragma unroll
+          for (int k = 0; k < kPer; ++k) {
+            const int i = ct + 128 * k, r = (i >> 3) & 63;
+            st[i] = r < nvalid ? make_uint4(bf16x2_to_h2(x[k].x), bf16x2_to_h2(x[k].y), bf16x2_to_h2(x[k].z),
+                                            bf16x2_to_h2(x[k].w))
+                               : make_uint4(0u, 0u, 0u, 0u);
+          }
+          ptx::fence_proxy_async_smem();
+        } else if (nvalid < 64) {
+#pragma unroll
+          for (int k = 0; k < kPer; ++k) {
+            const int i = ct + 128 * k, r = (i >> 3) & 63;
+            if (r >= nvalid) st[i] = make_uint4(0u, 0u, 0u, 0u);
+          }
+          ptx::fence_proxy_async_smem();
+        }
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive_cluster(full0_leader + 8 * rg.stage);
+        rg.advance();
       }
     }
   }
@@ -1033,6 +1209,150 @@ __device__ __forceinline__ float quantize_q(const Params& p, int v, uint32_t ran
   return s / a;
 }
 
+// ---------------------------------------------------------------------------
+// Cooperative merge of one sequence split between more than fuse_max pairs
+// (p.coop: every pair of the launch is resident).  The LSE combine of
+// mla_decode.py:212-246 over all of the sequence's pieces, spread over every CTA
+// of this rank that holds one: CTA k of n waits (bounded) until all n pieces of
+// its rank are published, then merges its contiguous share [o0, o1) of the rank's
+// 64 x 128 output quads (4 latent columns of one head): that share of every piece
+// is staged in the (idle) shared memory by one bulk copy per piece, all in flight
+// at once, while the weights of its heads are computed from the pieces' LSEs;
+// then each thread sums its quads over the pieces from shared memory.  Run by the
+// 4 softmax warps (L is the thread's index among them); `bar` / `ph` is their
+// 4-warp barrier, `mbar` / `mph` the staging barrier.
+// ---------------------------------------------------------------------------
+template <typename Out>
+__device__ __noinline__ bool coop_merge(const Params& p, const Ctx& c, const TileMap& tm, uint32_t rank, int pair,
+                                        uint8_t* smem, uint32_t bar, uint32_t& ph, uint32_t mbar, uint32_t& mph,
+                                        volatile uint32_t* flag, int L, int lane, int bb, int pf, int pl) {
+  auto sync4 = [&]() -> bool {
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive_local(bar);
+    const bool ok = wait_bar(c, bar, ph & 1u, kErrSoftmax);
+    ++ph;
+    return ok;
+  };
+  const int n = pl - pf + 1, k = pair - pf;
+  uint32_t* arrive = p.counters + 4 * bb + rank;
+  uint32_t* done = p.counters + 4 * bb + 2 + rank;
+  constexpr int kQuads = 64 * (kDim / 4);            // this rank's output quads
+  const int o0 = (int)((long long)k * kQuads / n), o1 = (int)((long long)(k + 1) * kQuads / n);
+  const int h_lo = o0 / (kDim / 4), nh = (o1 - 1) / (kDim / 4) - h_lo + 1;
+  const uint32_t chunk = (uint32_t)(o1 - o0) * 16u;   // bytes of this CTA's share of one piece
+  // the idle shared memory: every piece's share staged from offset 0 (at most
+  // 128 KB + 16 n bytes), the tables at kMergeTab
+  uint32_t* s_slot = reinterpret_cast<uint32_t*>(smem + kMergeTab);   // [n]
+  float* s_w = reinterpret_cast<float*>(s_slot + kMaxPairs);          // [n][nh], n * nh <= 64 + 2n
+  float* s_big = s_w + 64 + 2 * kMaxPairs;                             // [nh]
+  const float4* stage = reinterpret_cast<const float4*>(smem);
+  for (int q = L; q < n; q += 128) s_slot[q] = (uint32_t)pair_slot(tm, pf + q, bb);
+  if (L == 0) {
+    const uint64_t t0 = ptx::globaltimer();
+    uint32_t ok = 1u;
+    while (ptx::ld_acquire_gpu(arrive) < (uint32_t)n) {
+      if (aborted(c)) {
+        ok = 0u;
+        break;
+      }
+      if (ptx::globaltimer() - t0 > kTimeoutNs) {
+        raise_abort(c, kErrMerge);
+        ok = 0u;
+        break;
+      }
+      __nanosleep(32);
+    }
+    *flag = ok;
+  }
+  if (!sync4()) return false;
+  if (*flag == 0u) return false;
+  if (L == 0) {
+    // every piece's share in flight at once (bulk copies, one per piece)
+    ptx::fence_proxy_async_all();
+    ptx::mbar_arrive_expect_tx(mbar, (uint32_t)n * chunk);
+    const uint32_t dst = ptx::smem_u32(smem);
+    for (int q = 0; q < n; ++q)
+      ptx::bulk_load(dst + (uint32_t)q * chunk,
+                     p.part_o + ((size_t)s_slot[q] * kHeads + 64 * rank) * kDim + (size_t)o0 * 4, chunk, mbar);
+  }
+  // meanwhile: LSEs of this CTA's heads, then per head (one warp each, lanes over the
+  // pieces) the merged LSE and the pieces' weights, in place
+  for (int i = L; i < n * nh; i += 128) {
+    const int q = i / nh, hi = i - q * nh;
+    s_w[i] = __ldcg(p.part_lse + (size_t)s_slot[q] * kHeads + 64 * rank + h_lo + hi);
+  }
+  if (!sync4()) return false;
+  for (int hi = L >> 5; hi < nh; hi += 4) {
+    float mx = -INFINITY;
+    for (int q = lane; q < n; q += 32) mx = fmaxf(mx, s_w[q * nh + hi]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float sum = 0.f;
+    for (int q = lane; q < n; q += 32) sum += exp2f((s_w[q * nh + hi] - mx) * kLog2e);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    const float big = mx + logf(sum);
+    for (int q = lane; q < n; q += 32) s_w[q * nh + hi] = exp2f((s_w[q * nh + hi] - big) * kLog2e);
+    if (lane == 0) s_big[hi] = big;
+  }
+  if (!sync4()) return false;
+  if (!wait_bar(c, mbar, mph & 1u, kErrMerge)) return false;
+  ++mph;
+  const int oseq = vseq_seq(p, bb), h0 = vseq_head0(p, bb);
+  const int per = (int)(chunk / 16u);
+  for (int i = L; i < o1 - o0; i += 128) {
+    const int o = o0 + i, hr = o / (kDim / 4), col = 4 * (o % (kDim / 4));
+    const float* wq = s_w + (hr - h_lo);
+    // four independent sums over the pieces (no chain of dependent adds)
+    float4 a[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) a[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+    int q = 0;
+    for (; q + 4 <= n; q += 4) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float w = wq[(q + r) * nh];
+        const float4 v = stage[(q + r) * per + i];
+        a[r].x = fmaf(w, v.x, a[r].x);
+        a[r].y = fmaf(w, v.y, a[r].y);
+        a[r].z = fmaf(w, v.z, a[r].z);
+        a[r].w = fmaf(w, v.w, a[r].w);
+      }
+    }
+    for (; q < n; ++q) {
+      const float w = wq[q * nh];
+      const float4 v = stage[q * per + i];
+      a[0].x = fmaf(w, v.x, a[0].x);
+      a[0].y = fmaf(w, v.y, a[0].y);
+      a[0].z = fmaf(w, v.z, a[0].z);
+      a[0].w = fmaf(w, v.w, a[0].w);
+    }
+    const float4 acc = make_float4((a[0].x + a[1].x) + (a[2].x + a[3].x), (a[0].y + a[1].y) + (a[2].y + a[3].y),
+                                   (a[0].z + a[1].z) + (a[2].z + a[3].z), (a[0].w + a[1].w) + (a[2].w + a[3].w));
+    const int hglob = h0 + 64 * (int)rank + hr;
+    if (hglob < p.heads) {
+      const size_t orow = (size_t)oseq * p.heads + hglob;
+      if (p.out_f32)
+        *reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow * kDim + col) = acc;
+      else
+        *reinterpret_cast<uint2*>(static_cast<Out*>(p.out) + orow * kDim + col) =
+            make_uint2(pack2<Out>(acc.x, acc.y), pack2<Out>(acc.z, acc.w));
+      if (col == 0 && p.lse_out != nullptr) p.lse_out[orow] = s_big[hr - h_lo];
+    }
+  }
+  // every CTA of the rank counts itself done; the last one resets both counters for
+  // the next call (all others are past their waits by then)
+  if (!sync4()) return false;
+  if (L == 0) {
+    __threadfence();
+    if (atomicAdd(done, 1u) + 1u == (uint32_t)n) {
+      atomicExch(arrive, 0u);
+      atomicExch(done, 0u);
+    }
+  }
+  return true;
+}
+
 template <typename T>
 __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, uint32_t rank, int pair,
                                                  uint8_t* smem, uint32_t tmem, Barriers* bars, int wq,
@@ -1184,6 +1504,9 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
   const TileMap& tm = it.m;
   Piece pc;
   int piece = 0;
+  // sequences split between more than fuse_max pairs that this pair has a piece of
+  // (at most its first and its last piece), merged at the end in a cooperative launch
+  int n_wide = 0, wide_bb[2] = {0, 0}, wide_pf[2] = {0, 0}, wide_pl[2] = {0, 0};
   bool have = it.next(&pc);
   if (have && !take_qt(0, pc.bb)) return;
   while (have) {
@@ -1296,7 +1619,7 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
     ptx::tc_fence_after();
     int pf = 0, pl = 0;
     if (!pc.full) pairs_of_sequence(tm, pc.bb, &pf, &pl);
-    uint32_t* cnt = p.counters + 2 * pc.bb + rank;
+    uint32_t* cnt = p.counters + 4 * pc.bb + rank;
     const uint32_t npieces = (uint32_t)(pl - pf + 1);
     // sequences split between more pairs are left to the combine launch
     const bool fuse = npieces <= (uint32_t)p.fuse_max;
@@ -1337,6 +1660,23 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
           }
           if (!wait_leader()) return;
           merge = *merge_flag != 0u;
+        } else if (p.coop) {
+          // split between many pairs: counted here, merged by all of them together
+          // once every piece is published (after each pair's last piece, below)
+          __threadfence();
+          if (!sync4(stg, n_stg)) return;
+          if (L == 0) {
+            ptx::bulk_wait();
+            ptx::fence_proxy_async_all();
+            __threadfence();
+            atomicAdd(cnt, 1u);
+          }
+          if (n_wide < 2) {
+            wide_bb[n_wide] = pc.bb;
+            wide_pf[n_wide] = pf;
+            wide_pl[n_wide] = pl;
+            ++n_wide;
+          }
         }
         // else: a combine launch after this kernel merges the sequence
       } else if (L == 0) {
@@ -1470,13 +1810,24 @@ __device__ __forceinline__ void softmax_epilogue(const Params& p, const Ctx& c, 
     pc = nxt;
     have = has_next;
   }
+
+  // ---- cooperative merge of the sequences split between many pairs (p.coop only):
+  // out of line, so that its load streams do not weigh on the registers of the
+  // per-tile loop above
+  for (int w = 0; w < n_wide; ++w)
+    if (!coop_merge<Out>(p, c, tm, rank, pair, smem, lx, n_lx, mload, n_stage, merge_flag, L, lane, wide_bb[w],
+                         wide_pf[w], wide_pl[w]))
+      return;
 }
 
 // ---------------------------------------------------------------------------
 // the kernel: warp 0 K producer, warp 1 TMEM owner + QK^T issuer, warp 2 V
 // producer, warp 3 P.V issuer, warps 4..7 softmax/epilogue, warp 8 Q loader
 // (warps 9..11 complete the third warpgroup).  For an FP8 cache the block has
-// 16 warps: warp 2 also prefetches Q, and warps 8..15 convert V to fp16.
+// 16 warps: warp 2 also prefetches Q, and warps 8..15 convert V to fp16.  The
+// Cv variant has 16 warps too: warps 12..15 rewrite each landed V stage (tail
+// rows zeroed, bf16 -> fp16 with kF16); warps 9..11 are idle.  In the plain
+// variants warp 9 zeroes the tail rows of a sequence's last V units.
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_of<T>(), 1)
@@ -1495,7 +1846,7 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
 
   if (threadIdx.x == 0) {
     // V operand stages: one expect-tx arrival (TMA), or FP8: kConvWarps converter warps x 2 CTAs
-    const uint32_t n_vfull = Io<T>::kKv8 ? 2u * kConvWarps : 1u;
+    const uint32_t n_vfull = Io<T>::kKv8 ? 2u * kConvWarps : (Io<T>::kConv ? 2u * kFixWarps : 1u);
     for (int s = 0; s < 8; ++s) {
       ptx::mbar_init(ptx::smem_u32(&bars->kfull[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&bars->kempty[s]), 1);
@@ -1505,6 +1856,7 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
     for (int s = 0; s < 8; ++s) {
       ptx::mbar_init(ptx::smem_u32(&bars->v8full[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&bars->v8empty[s]), kConvWarps);
+      ptx::mbar_init(ptx::smem_u32(&bars->vfix[s]), 2);
     }
     ptx::mbar_init(ptx::smem_u32(&bars->q_full), 1);
     ptx::mbar_init(ptx::smem_u32(&bars->q_empty), 1);
@@ -1587,6 +1939,10 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
   } else if (Io<T>::kKv8 && warp >= 8) {
     // FP8: warps 8..15 dequantize the V units
     v_converter<T>(p, c, pair, smem, bars, (warp - 8) * 32 + lane, lane);
+  } else if (warp == 9 && !Io<T>::kKv8 && !Io<T>::kConv) {
+    v_tailfix<T>(p, c, rank, pair, smem, bars, lane);
+  } else if (warp >= 12) {
+    if constexpr (Io<T>::kConv) v_fix<T>(p, c, pair, smem, bars, (warp - 12) * 32 + lane, lane);
   }
   }
   __syncwarp();
@@ -1848,6 +2204,7 @@ bool make_map_kv(CUtensorMap* m, const void* base, uint64_t cols, uint64_t kv_he
 struct DeviceInfo {
   bool ready = false;
   int max_pairs = 0;
+  bool coop = false;   // cooperative launches available (in-kernel merge of wide splits)
 };
 DeviceInfo g_dev[64];
 std::mutex g_dev_mutex;
@@ -1875,21 +2232,29 @@ cudaError_t device_info(int dev, DeviceInfo* out) {
   std::lock_guard<std::mutex> lock(g_dev_mutex);
   DeviceInfo& d = g_dev[dev];
   if (!d.ready) {
-    int n[4] = {0, 0, 0, 0};
+    int n[5] = {0, 0, 0, 0, 0};
     cudaError_t err = set_attrs_and_count<__nv_bfloat16>(&n[0]);
     if (err == cudaSuccess) err = set_attrs_and_count<__half>(&n[1]);
     if (err == cudaSuccess) err = set_attrs_and_count<Kv8<__nv_bfloat16>>(&n[2]);
     if (err == cudaSuccess) err = set_attrs_and_count<Kv8<__half>>(&n[3]);
+    if (err == cudaSuccess) err = set_attrs_and_count<Cv<__nv_bfloat16, true>>(&n[4]);
     if (err != cudaSuccess) return err;
     d.max_pairs = n[0];
-    for (int i = 1; i < 4; ++i) d.max_pairs = n[i] < d.max_pairs ? n[i] : d.max_pairs;
+    for (int i = 1; i < 5; ++i) d.max_pairs = n[i] < d.max_pairs ? n[i] : d.max_pairs;
+    int coop = 0;
+    if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess) {
+      cudaGetLastError();
+      coop = 0;
+    }
+    d.coop = coop != 0;
     d.ready = true;
   }
   *out = d;
   return cudaSuccess;
 }
 
-int current_max_pairs() {
+int current_max_pairs(bool* coop = nullptr) {
+  if (coop != nullptr) *coop = false;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   DeviceInfo d;
@@ -1897,6 +2262,7 @@ int current_max_pairs() {
     cudaGetLastError();   // clear a sticky-free error from the query
     return 0;
   }
+  if (coop != nullptr) *coop = d.coop;
   return d.max_pairs;
 }
 
@@ -1936,8 +2302,12 @@ SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int
   const int nt = (seqlen_kv + sm100::kTile - 1) / sm100::kTile;
   const long long total = (long long)batch * nt;
   int pairs = cfg.num_split > 0 ? cfg.num_split : 0;
-  int cap = sm100::current_max_pairs();
-  if (cap <= 0) cap = 74;   // planning on a host without a usable GPU
+  bool coop = false;
+  int cap = sm100::current_max_pairs(&coop);
+  if (cap <= 0) {
+    cap = 74;     // planning on a host without a usable GPU: a B200's plan
+    coop = true;
+  }
   if (pairs == 0 || pairs > cap) pairs = cap;
   if (pairs > sm100::kMaxPairs) pairs = sm100::kMaxPairs;
   if (cfg.num_split <= 0) {
@@ -1971,8 +2341,58 @@ SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int
     const long long pz = ((x0 + nt) * pairs + total - 1) / total - 1;
     if (pz - pf + 1 > most) most = (int)(pz - pf + 1);
   }
-  *variant = most > sm100::kFuseMaxPieces ? 1 : 0;
+  // sequences split between many pairs: merged by the combine launch (variant 1;
+  // measured faster on B200: b1 s131072 77.6 against 94.1 us per call, b16 s8192
+  // 95 against 124 us), or, when the config asks for it (combine_groups < 0), by
+  // all of their pairs inside the decode launch (variant 2, cooperative launch)
+  const bool in_kernel = cfg.combine_groups < 0;
+  *variant = most > sm100::kFuseMaxPieces ? ((coop && in_kernel) ? 2 : 1) : 0;
   return pl;
+}
+
+bool sm100_coop_available() {
+  bool coop = false;
+  if (sm100::current_max_pairs(&coop) <= 0) return true;   // host without a GPU: a B200's plan
+  return coop;
+}
+
+// One launch of the decode kernel variant K: cooperative (every CTA resident at
+// once, which the in-kernel merge of wide splits waits on) when p.coop is set.
+template <typename K>
+cudaError_t launch_variant(const sm100::Params& p, int pairs, cudaStream_t stream) {
+  using namespace sm100;
+  if (!p.coop) {
+    mla_sm100_decode_kernel<K><<<2 * pairs, threads_of<K>(), Smem<K>::kBytes, stream>>>(p);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(threads_of<K>(), 1, 1);
+  cfg.dynamicSmemBytes = Smem<K>::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeCooperative;
+  attr.val.cooperative = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, mla_sm100_decode_kernel<K>, p);
+}
+
+cudaError_t launch_sm100_combine(const DecodeArgs& a);
+
+cudaError_t launch_sm100_decode_plain_then_combine(const DecodeArgs& a, const sm100::Params& p) {
+  using namespace sm100;
+  const int pairs = a.plan.bpc;
+  cudaError_t err;
+  if (a.kv_fp8)
+    err = a.dtype == MLA_DTYPE_BF16 ? launch_variant<Kv8<__nv_bfloat16>>(p, pairs, a.stream)
+                                    : launch_variant<Kv8<__half>>(p, pairs, a.stream);
+  else if (a.dtype == MLA_DTYPE_BF16)
+    err = kConvV ? launch_variant<Cv<__nv_bfloat16, true>>(p, pairs, a.stream)
+                 : launch_variant<__nv_bfloat16>(p, pairs, a.stream);
+  else
+    err = launch_variant<__half>(p, pairs, a.stream);
+  return err == cudaSuccess ? launch_sm100_combine(a) : err;
 }
 
 cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
@@ -1999,14 +2419,17 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
       !make_map3(&p.tm_q, a.q, kDim, qs.g, qs.qb, dt) || !make_map3(&p.tm_qpe, a.q_pe, kPeDim, qs.g, qs.qb, dt))
     return cudaErrorInvalidValue;
   p.out_f32 = a.out_dtype == MLA_DTYPE_F32 ? 1 : 0;
-  (void)variant;   // the combine launch (variant 1, ragged calls) takes what the kernel does not merge
+  // variant 1: the combine launch takes what the kernel does not merge; variant 2:
+  // a cooperative launch merges every split sequence in the kernel
   p.fuse_max = kFuseMaxPieces;
+  p.coop = (variant == 2 && info.coop) ? 1 : 0;
   if (!(p.out_f32 ? make_map3(&p.tm_out, a.out, kDim, qs.g, qs.qb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4)
                   : make_map3(&p.tm_out, a.out, kDim, qs.g, qs.qb, dt)))
     return cudaErrorInvalidValue;
   if (a.part_o != nullptr &&
       !make_map(&p.tm_part, a.part_o, kDim, (uint64_t)a.plan.part_rows, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4))
     return cudaErrorInvalidValue;
+  p.kv = static_cast<const uint8_t*>(a.kv);
   p.q = static_cast<const uint8_t*>(a.q);
   p.qpe = static_cast<const uint8_t*>(a.q_pe);
   p.out = a.out;
@@ -2032,21 +2455,24 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
   p.page_size = a.page_size;
   p.max_pages = a.max_pages;
   p.kv_scale = a.kv_fp8 ? a.kv_scale : 1.f;
+  cudaError_t lerr;
   if (a.kv_fp8) {
-    if (a.dtype == MLA_DTYPE_BF16)
-      mla_sm100_decode_kernel<Kv8<__nv_bfloat16>><<<2 * pairs, threads_of<Kv8<__nv_bfloat16>>(),
-                                                    Smem<Kv8<__nv_bfloat16>>::kBytes, a.stream>>>(p);
-    else
-      mla_sm100_decode_kernel<Kv8<__half>>
-          <<<2 * pairs, threads_of<Kv8<__half>>(), Smem<Kv8<__half>>::kBytes, a.stream>>>(p);
+    lerr = a.dtype == MLA_DTYPE_BF16 ? launch_variant<Kv8<__nv_bfloat16>>(p, pairs, a.stream)
+                                     : launch_variant<Kv8<__half>>(p, pairs, a.stream);
   } else if (a.dtype == MLA_DTYPE_BF16) {
-    mla_sm100_decode_kernel<__nv_bfloat16>
-        <<<2 * pairs, threads_of<__nv_bfloat16>(), Smem<__nv_bfloat16>::kBytes, a.stream>>>(p);
+    lerr = kConvV ? launch_variant<Cv<__nv_bfloat16, true>>(p, pairs, a.stream)
+                  : launch_variant<__nv_bfloat16>(p, pairs, a.stream);
   } else {
-    mla_sm100_decode_kernel<__half>
-        <<<2 * pairs, threads_of<__half>(), Smem<__half>::kBytes, a.stream>>>(p);
+    lerr = launch_variant<__half>(p, pairs, a.stream);
   }
-  return cudaGetLastError();
+  if (lerr != cudaSuccess && p.coop) {
+    // the cooperative launch was refused: the plain launch, and the combine launch
+    // merges what the kernel then leaves
+    cudaGetLastError();
+    p.coop = 0;
+    return launch_sm100_decode_plain_then_combine(a, p);
+  }
+  return lerr;
 }
 
 cudaError_t launch_wait_selftest(uint32_t* status, unsigned long long* result, uint64_t limit_ns,

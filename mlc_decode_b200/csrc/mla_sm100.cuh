@@ -17,9 +17,18 @@ bool sm100_supports_ext(int batch, int q_len, int heads, int kv_heads, int seqle
 QShape qshape(const DecodeArgs& a);
 
 // Split plan (and kernel variant) the tensor-core kernel uses for this shape.
+// Variant 0: every sequence is whole in one CTA pair or split between at most 3
+// and merged in the kernel; 1: some sequence is split between more pairs and a
+// combine launch merges it; 2: such sequences are merged in the kernel by all
+// their pairs together (cooperative launch; one launch per call).
 SplitPlan sm100_plan(int batch, int heads, int seqlen_kv, const MlaCfg& cfg, int* variant);
 
+// True when the current device takes cooperative launches (variant 2).
+bool sm100_coop_available();
+
 // Enqueue the tensor-core split-KV kernel; partials go to a.part_o/a.part_lse.
+// Variant 2 launches cooperatively; if the driver refuses that launch, the plain
+// launch and the combine launch run instead (same result).
 cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant);
 
 // Plan of a ragged call (per-sequence lengths): max_seqlen_kv bounds every length.

@@ -261,26 +261,33 @@ def test_sequence_split_emulated_on_one_gpu(world, cuda):
     assert res["ok"], res
 
 
-@pytest.mark.parametrize("b,s", [(1, 32768), (2, 20000)])
-def test_many_piece_sequences_use_the_combine_launch(b, s, cuda):
-    """A sequence split between many CTA pairs is merged by a second launch."""
+@pytest.mark.parametrize("cfg", [None, {"combine_groups": 2}, {"combine_groups": -1}],
+                         ids=["default", "combine_launch", "in_kernel"])
+@pytest.mark.parametrize("b,s,dt", [(1, 32768, "bf16"), (2, 20000, "bf16"), (16, 8192, "fp16"), (3, 5000, "bf16")])
+def test_many_piece_sequences(b, s, dt, cfg, cuda):
+    """Sequences split between many CTA pairs: merged by a second (combine) launch, or,
+    with combine_groups < 0, by all of their pairs inside the decode launch (a
+    cooperative launch, one launch per call)."""
     from mlc_decode_b200 import MlaDecodeKernel
 
-    k = MlaDecodeKernel(b, 128, 1, s)
-    plan = k.plan(torch.bfloat16)
-    assert plan["kernel"] == "tc" and plan["launches"] == 2, plan
-    inputs = O.make_inputs(b, 128, s, "bf16", seed=51)
-    out, lse = run_decode(inputs)
+    in_kernel = cfg is not None and cfg["combine_groups"] < 0
+    k = MlaDecodeKernel(b, 128, 1, s, cfg=cfg)
+    plan = k.plan(TDT[dt])
+    assert plan["kernel"] == "tc" and plan["launches"] == (1 if in_kernel else 2), plan
+    inputs = O.make_inputs(b, 128, s, dt, seed=51)
+    out, lse = run_decode(inputs, cfg)
     ref, ref_lse = O.ref_program_f64(*inputs)
-    res = O.check_parity(out, lse, ref, ref_lse, "bf16")
+    res = O.check_parity(out, lse, ref, ref_lse, dt)
     assert res["ok"], res
-    # and the float32 variant through the same launches
+    # and the float32 variant through the same launches, twice (counters reset)
     q, q_pe, kv, k_pe = (t.cuda() for t in inputs)
-    o = torch.empty(b, 128, 512, device="cuda")
-    l32 = torch.empty(b, 128, device="cuda")
-    k.partial(q, q_pe, kv, k_pe, o, l32)
-    torch.cuda.synchronize()
-    _f32_check(o.cpu().numpy(), l32.cpu().numpy(), ref, ref_lse)
+    for _ in range(2):
+        o = torch.full((b, 128, 512), float("nan"), device="cuda")
+        l32 = torch.full((b, 128), float("nan"), device="cuda")
+        k.partial(q, q_pe, kv, k_pe, o, l32)
+        torch.cuda.synchronize()
+        _f32_check(o.cpu().numpy(), l32.cpu().numpy(), ref, ref_lse)
+    assert k.device_status(q.device, TDT[dt]) == 0
 
 
 def test_combine_float32_output(cuda):

@@ -8,9 +8,10 @@ C ABI twice in a row (different inputs each time, so a stale result left in
 the shared array would show) and compares each result with the regular
 workspace-taking entry point, mla_decode_fwd, and with the float64 oracle on
 sampled sequences, within the parity tolerances the other tests use.  The
-cases cover both kernels and both ways the tensor-core kernel merges a split
-sequence (in the kernel, through the status word and piece counters the
-entry point clears in the shared array, and in a second combine launch).
+cases cover both kernels and every way the tensor-core kernel merges a split
+sequence (in the kernel by the last of a few pairs or by all pairs of a wide
+split, through the status word and piece counters the entry point clears in
+the shared array, and in a second combine launch).
 This file is collected last on purpose.
 """
 import ctypes
@@ -27,11 +28,13 @@ pytestmark = pytest.mark.gpu
 SCRATCH = 8 << 20
 
 # (name, batch, heads, kv_ctx, cfg, expected tensor-core merge: None = CUDA-core kernel,
-#  0 = whole sequences or merged in the kernel, 1 = combine launch)
+#  0 = whole sequences or merged in the kernel (by the last of <= 3 pairs, or by all
+#  pairs of a wide split in a cooperative launch), 1 = combine launch)
 CASES = [
     ("simt_8_splits", 2, 128, 4096, {"kernel": "simt", "num_split": 8}, None),
     ("tc_whole_sequences", 64, 128, 8192, {"kernel": "tc"}, 0),
     ("tc_merged_in_kernel", 2, 128, 4096, {"kernel": "tc", "num_split": 4}, 0),
+    ("tc_merged_by_all_pairs", 1, 128, 32768, {"kernel": "tc", "num_split": 12, "combine_groups": -1}, 0),
     ("tc_combine_launch", 1, 128, 32768, {"kernel": "tc", "num_split": 12}, 1),
 ]
 
@@ -88,7 +91,7 @@ def test_noalloc_matches_workspace_entry_point_and_oracle_twice(cuda, name, b, h
 
 def test_noalloc_status_reads_zero_after_a_call(cuda):
     cfg = capi.make_cfg({"kernel": "tc"})
-    b, h, s = 2, 128, 1024
+    b, h, s = 64, 128, 1024   # whole sequences per CTA pair: the workspace is the header only
     q, q_pe, kv, k_pe = (t.to(cuda) for t in O.make_inputs(b, h, s, "bf16", seed=5))
     out = torch.empty_like(q)
     stream = torch.cuda.current_stream().cuda_stream
