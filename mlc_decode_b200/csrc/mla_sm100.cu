@@ -53,6 +53,8 @@
 #include <cudaTypedefs.h>
 #include <math.h>
 
+#include <string.h>
+
 #include <mutex>
 #include <type_traits>
 
@@ -2395,6 +2397,84 @@ cudaError_t launch_sm100_decode_plain_then_combine(const DecodeArgs& a, const sm
   return err == cudaSuccess ? launch_sm100_combine(a) : err;
 }
 
+namespace sm100 {
+
+// The six tensor maps of a call, encoded by the driver (cuTensorMapEncodeTiled, a
+// few microseconds of host time for all of them) or taken from a small per-thread
+// cache of the last calls' maps: a decode loop calls again and again with the same
+// tensors, and a map depends only on the key below.
+struct MapKey {
+  const void *q, *q_pe, *kv, *k_pe, *out, *part_o;
+  long long part_rows, kv_rows;
+  int g, qb, kv_heads, dtype, out_f32, kv_fp8;
+  bool operator==(const MapKey& o) const { return memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap kv, kpe, q, qpe, out, part;
+};
+
+bool tensor_maps(const DecodeArgs& a, const QShape& qs, Params* p) {
+  MapKey key;
+  memset(&key, 0, sizeof(key));   // padding included: keys compare bytewise
+  key.q = a.q;
+  key.q_pe = a.q_pe;
+  key.kv = a.kv;
+  key.k_pe = a.k_pe;
+  key.out = a.out;
+  key.part_o = a.part_o;
+  key.part_rows = a.part_o != nullptr ? a.plan.part_rows : 0;
+  key.kv_rows = a.block_table != nullptr ? (long long)a.num_pages * a.page_size : (long long)a.batch * a.seqlen_kv;
+  key.g = qs.g;
+  key.qb = qs.qb;
+  key.kv_heads = qs.kv_heads;
+  key.dtype = a.dtype;
+  key.out_f32 = p->out_f32;
+  key.kv_fp8 = a.kv_fp8;
+  constexpr int kSlots = 8;
+  thread_local MapEntry cache[kSlots];
+  thread_local int filled = 0, next = 0;
+  for (int i = 0; i < filled; ++i) {
+    if (cache[i].key == key) {
+      p->tm_kv = cache[i].kv;
+      p->tm_kpe = cache[i].kpe;
+      p->tm_q = cache[i].q;
+      p->tm_qpe = cache[i].qpe;
+      p->tm_out = cache[i].out;
+      p->tm_part = cache[i].part;
+      return true;
+    }
+  }
+  const CUtensorMapDataType dt =
+      a.dtype == MLA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uint64_t kv_rows = (uint64_t)key.kv_rows;
+  const bool ok_kv = a.kv_fp8 ? make_map_kv(&p->tm_kv, a.kv, kDim, qs.kv_heads, kv_rows,
+                                            CU_TENSOR_MAP_DATA_TYPE_UINT8, 1)
+                               : make_map_kv(&p->tm_kv, a.kv, kDim, qs.kv_heads, kv_rows, dt);
+  if (!ok_kv || !make_map_kv(&p->tm_kpe, a.k_pe, kPeDim, qs.kv_heads, kv_rows, dt) ||
+      !make_map3(&p->tm_q, a.q, kDim, qs.g, qs.qb, dt) || !make_map3(&p->tm_qpe, a.q_pe, kPeDim, qs.g, qs.qb, dt))
+    return false;
+  if (!(p->out_f32 ? make_map3(&p->tm_out, a.out, kDim, qs.g, qs.qb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4)
+                   : make_map3(&p->tm_out, a.out, kDim, qs.g, qs.qb, dt)))
+    return false;
+  if (a.part_o != nullptr &&
+      !make_map(&p->tm_part, a.part_o, kDim, (uint64_t)a.plan.part_rows, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4))
+    return false;
+  MapEntry& e = cache[next];
+  e.key = key;
+  e.kv = p->tm_kv;
+  e.kpe = p->tm_kpe;
+  e.q = p->tm_q;
+  e.qpe = p->tm_qpe;
+  e.out = p->tm_out;
+  e.part = p->tm_part;
+  next = (next + 1) % kSlots;
+  if (filled < kSlots) ++filled;
+  return true;
+}
+
+}  // namespace sm100
+
 cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
   using namespace sm100;
   int dev = 0;
@@ -2407,28 +2487,13 @@ cudaError_t launch_sm100_decode(const DecodeArgs& a, int variant) {
   const int pairs = a.plan.bpc;
   if (pairs < 1 || pairs > info.max_pairs) return cudaErrorInvalidConfiguration;
   Params p{};
-  const CUtensorMapDataType dt =
-      a.dtype == MLA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const uint64_t kv_rows = a.block_table != nullptr ? (uint64_t)a.num_pages * a.page_size
-                                                    : (uint64_t)a.batch * a.seqlen_kv;
   const QShape qs = qshape(a);
-  const bool ok_kv = a.kv_fp8 ? make_map_kv(&p.tm_kv, a.kv, kDim, qs.kv_heads, kv_rows,
-                                            CU_TENSOR_MAP_DATA_TYPE_UINT8, 1)
-                               : make_map_kv(&p.tm_kv, a.kv, kDim, qs.kv_heads, kv_rows, dt);
-  if (!ok_kv || !make_map_kv(&p.tm_kpe, a.k_pe, kPeDim, qs.kv_heads, kv_rows, dt) ||
-      !make_map3(&p.tm_q, a.q, kDim, qs.g, qs.qb, dt) || !make_map3(&p.tm_qpe, a.q_pe, kPeDim, qs.g, qs.qb, dt))
-    return cudaErrorInvalidValue;
   p.out_f32 = a.out_dtype == MLA_DTYPE_F32 ? 1 : 0;
   // variant 1: the combine launch takes what the kernel does not merge; variant 2:
   // a cooperative launch merges every split sequence in the kernel
   p.fuse_max = kFuseMaxPieces;
   p.coop = (variant == 2 && info.coop) ? 1 : 0;
-  if (!(p.out_f32 ? make_map3(&p.tm_out, a.out, kDim, qs.g, qs.qb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4)
-                  : make_map3(&p.tm_out, a.out, kDim, qs.g, qs.qb, dt)))
-    return cudaErrorInvalidValue;
-  if (a.part_o != nullptr &&
-      !make_map(&p.tm_part, a.part_o, kDim, (uint64_t)a.plan.part_rows, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4))
-    return cudaErrorInvalidValue;
+  if (!tensor_maps(a, qs, &p)) return cudaErrorInvalidValue;
   p.kv = static_cast<const uint8_t*>(a.kv);
   p.q = static_cast<const uint8_t*>(a.q);
   p.qpe = static_cast<const uint8_t*>(a.q_pe);

@@ -74,6 +74,9 @@ class MlaDecodeKernel:
         capi.load()   # fail loudly now if the library is unusable
         self._ws = {}
         self._lock = threading.Lock()
+        b, h, s = self.batch, self.heads, self.seqlen_kv
+        self._shapes = (torch.Size((b, h, DIM)), torch.Size((b, h, PE_DIM)), torch.Size((b, s, 1, DIM)),
+                        torch.Size((b, s, 1, PE_DIM)))
 
     # -- workspace ---------------------------------------------------------
     def workspace_bytes(self, dtype: torch.dtype) -> int:
@@ -113,18 +116,19 @@ class MlaDecodeKernel:
         if dtype not in _DTYPES:
             raise ValueError(f"q must be float16 or bfloat16, got {dtype}")
         dev = q.device
-        _check_tensor("q", q, (b, h, DIM), dtype, None)
-        _check_tensor("q_pe", q_pe, (b, h, PE_DIM), dtype, dev)
-        _check_tensor("kv", kv, (b, s, 1, DIM), dtype, dev)
-        _check_tensor("k_pe", k_pe, (b, s, 1, PE_DIM), dtype, dev)
-        _check_tensor("out", out, (b, h, DIM), dtype, dev)
+        shapes = self._shapes
+        # one pass over the tensors; the detailed checker only runs to explain a failure
+        for name, t, shape in (("q", q, shapes[0]), ("q_pe", q_pe, shapes[1]), ("kv", kv, shapes[2]),
+                               ("k_pe", k_pe, shapes[3]), ("out", out, shapes[0])):
+            if not (type(t) is torch.Tensor and t.dtype == dtype and t.device == dev and t.shape == shape
+                    and t.is_contiguous() and dev.type == "cuda"):
+                _check_tensor(name, t, shape, dtype, dev)
         lse_ptr = None
         if lse is not None:
             _check_tensor("lse", lse, (b, h), torch.float32, dev)
             lse_ptr = lse.data_ptr()
         ws = self._workspace(dev, dtype)
-        with torch.cuda.device(dev):
-            stream = torch.cuda.current_stream(dev).cuda_stream
+        stream = torch.cuda.current_stream(dev).cuda_stream
         capi.decode_fwd(q.data_ptr(), q_pe.data_ptr(), kv.data_ptr(), k_pe.data_ptr(), out.data_ptr(),
                         lse_ptr, ws.data_ptr(), ws.numel(), b, h, s, _DTYPES[dtype], self._ccfg, stream)
 
