@@ -88,6 +88,8 @@ def parse_args():
                     help="decode through mla_decode_fp8kv: e4m3 latent cache (scale 1/16), rope in --dtype")
     ap.add_argument("--ragged", action="store_true",
                     help="with --paged: per-sequence lengths drawn uniformly from [1, kv_ctx] (seeded)")
+    ap.add_argument("--seq-exchange", choices=["auto", "p2p", "collective"], default="auto",
+                    help="--seq-split under torchrun: the exchange of the ranks' (O, LSE) blocks")
     ap.add_argument("--seq-split", action="store_true",
                     help="long-context sequence split: every sequence's KV rows split across the ranks, "
                          "(O, LSE) all-gathered over NCCL and merged")
@@ -109,8 +111,10 @@ def workload_name(a):
         name += ", FP8 (e4m3) latent KV cache"
     if a.seq_split:
         name = f"mla_decode b{a.batch} h{a.heads} s{a.kv_ctx} {a.dtype} (dim 512+64, kv_heads 1), "
-        name += (f"KV rows split across {a.gpus} GPU(s), (O, LSE) merged over NCCL" if a.gpus > 1
-                 else "whole sequence on one GPU (the sequence split's 1-GPU point)")
+        how = {"collective": "all-gathered over NCCL", "p2p": "pushed over NVLink peer memory",
+               "auto": "exchanged over NVLink peer memory (NCCL all-gather where peers are not reachable)"}
+        name += (f"KV rows split across {a.gpus} GPU(s), (O, LSE) {how[a.seq_exchange]} and merged"
+                 if a.gpus > 1 else "whole sequence on one GPU (the sequence split's 1-GPU point)")
     return name
 
 
@@ -123,7 +127,7 @@ def config_of(a, world, kv_bytes=None, flushed=None):
         flushed = kv_bytes < 2 * L2_BYTES
     return {"workload": workload_name(a), "batch_per_gpu": a.batch, "global_batch": a.batch * (1 if a.seq_split else world),
             "heads": a.heads, "kv_ctx": a.kv_ctx, "kernel": a.kernel, "num_split": a.num_split or "auto",
-            "parallelism": (f"sequence split over {world} GPU(s): NCCL all-gather of (O, LSE), LSE merge"
+            "parallelism": (f"sequence split over {world} GPU(s): exchange of (O, LSE) ({a.seq_exchange}), LSE merge"
                             if a.seq_split and world > 1 else f"batch split over {world} GPU(s), no collective"),
             "l2": ("inputs (KV+K_pe %.0f MB per GPU) larger than the 126 MB L2; no flush" % (kv_bytes / 1e6)
                    if not flushed else
@@ -371,7 +375,7 @@ def run_ours(a, rank, world, local_rank):
         gq = torch.Generator(device=dev).manual_seed(1234)
         q = torch.randn(b, h, 512, device=dev, generator=gq).to(tdt)
         q_pe = torch.randn(b, h, 64, device=dev, generator=gq).to(tdt)
-        dec = SequenceSplitDecoder(b, h, s, cfg=cfg)
+        dec = SequenceSplitDecoder(b, h, s, cfg=cfg, exchange=a.seq_exchange)
         lens = [dec.local_len] * b
         kv = torch.randn(b, dec.local_len, 1, 512, device=dev, generator=g).to(tdt)
         k_pe = torch.randn(b, dec.local_len, 1, 64, device=dev, generator=g).to(tdt)
@@ -384,7 +388,7 @@ def run_ours(a, rank, world, local_rank):
                 dec.local(q_, qp_, kv_, kp_)       # this rank's partial decode
 
             def combine_ws(self, out_):
-                dec.merge(out_)                    # NCCL all-gather of (O, LSE) + merge
+                dec.merge(out_)                    # exchange of (O, LSE) blocks + merge
 
         kern = _Seq()
         probe_obj = dec.kernel

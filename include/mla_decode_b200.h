@@ -181,6 +181,33 @@ int32_t mla_combine_strided(const float* part_lse, int64_t lse_split_stride,
                             void* out, float* lse, int32_t dtype, void* stream);
 
 /*
+ * The sequence split's exchange over NVLink, without a collective library (no
+ * reference counterpart: the reference has no multi-GPU path).  world (2..8)
+ * ranks, one GPU each on one node, each own a gather buffer of
+ * mla_seqsplit_buffer_bytes(world, batch, heads) bytes (256-byte aligned, zeroed
+ * once) and map every peer's buffer with mla_ipc_export / mla_ipc_import (CUDA
+ * IPC; handles exchanged by the host, e.g. over the process group).  Layout of
+ * a buffer: float blocks [2][world][chunk] with chunk = batch*heads*512 +
+ * round_up(batch*heads, 64): block [epoch & 1][r] is rank r's (O, LSE) of call
+ * `epoch` (O rows, then the LSEs); then a 256-byte header (flags, a counter, the
+ * status word at byte 68: 0, or 0x201 when a wait gave up).
+ * For call `epoch` (1, 2, 3, ... the same on every rank), rank `rank` writes its
+ * block [epoch & 1][rank] in its own buffer (mla_decode_partial into it), then
+ * mla_seqsplit_exchange enqueues one launch that stores that block into every
+ * peer's buffer, flags it there, and waits (at most 2 s) until every peer's block
+ * has arrived in this rank's buffer; mla_combine_strided over the blocks
+ * [epoch & 1][*] then merges them.  bufs holds every rank's buffer as mapped in
+ * this process (bufs[rank] its own).  The launch waits on the other GPUs' launches:
+ * every rank must make the call.
+ */
+size_t mla_seqsplit_buffer_bytes(int32_t world, int32_t batch, int32_t heads);
+int32_t mla_ipc_export(const void* ptr, void* handle_out /* 64 bytes */, uint64_t* offset_out);
+int32_t mla_ipc_import(const void* handle /* 64 bytes */, uint64_t offset, void** ptr_out);
+int32_t mla_ipc_close(void* ptr, uint64_t offset);
+int32_t mla_seqsplit_exchange(void* const* bufs, int32_t world, int32_t rank, uint32_t epoch,
+                              int32_t batch, int32_t heads, void* stream);
+
+/*
  * mla_decode_fwd for one contiguous part of every sequence's KV cache, with a
  * float32 result: o[b,h,:] (float32 [batch, heads, 512], normalised) and
  * lse[b,h] (float32 [batch, heads], natural log, required) are the decode of

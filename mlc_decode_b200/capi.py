@@ -28,7 +28,9 @@ EXPORTED_SYMBOLS = ("mla_abi_version", "mla_last_error", "mla_split_plan",
                     "mla_describe_plan", "mla_decode_partial", "mla_paged_workspace_bytes",
                     "mla_decode_paged", "mla_decode_ext_workspace_bytes", "mla_decode_ext",
                     "mla_decode_fp8kv", "mla_decode_ext_fp8kv", "mla_selftest_wait_timeout",
-                    "mla_noalloc_init", "mla_noalloc_status", "mla_combine_strided")
+                    "mla_noalloc_init", "mla_noalloc_status", "mla_combine_strided",
+                    "mla_seqsplit_buffer_bytes", "mla_ipc_export", "mla_ipc_import", "mla_ipc_close",
+                    "mla_seqsplit_exchange")
 
 MLA_SELFTEST_STATUS = 0x1FF   # status word written by mla_selftest_wait_timeout
 
@@ -125,6 +127,17 @@ def load(build_if_missing: bool = True):
         lib.mla_noalloc_init.restype = i32
         lib.mla_noalloc_status.argtypes = [vp, vp]
         lib.mla_noalloc_status.restype = i32
+        lib.mla_seqsplit_buffer_bytes.argtypes = [i32, i32, i32]
+        lib.mla_seqsplit_buffer_bytes.restype = sz
+        lib.mla_ipc_export.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint64)]
+        lib.mla_ipc_export.restype = i32
+        lib.mla_ipc_import.argtypes = [vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
+        lib.mla_ipc_import.restype = i32
+        lib.mla_ipc_close.argtypes = [vp, ctypes.c_uint64]
+        lib.mla_ipc_close.restype = i32
+        lib.mla_seqsplit_exchange.argtypes = [ctypes.POINTER(ctypes.c_void_p), i32, i32, ctypes.c_uint32, i32, i32,
+                                              vp]
+        lib.mla_seqsplit_exchange.restype = i32
         _lib = lib
         return lib
 
@@ -297,3 +310,36 @@ def noalloc_init() -> None:
 def noalloc_status(status_out, stream) -> None:
     """mla_noalloc_status: enqueue a copy of the static array's status word to ``status_out``."""
     check(load().mla_noalloc_status(status_out, stream))
+
+
+def seqsplit_buffer_bytes(world, batch, heads) -> int:
+    n = load().mla_seqsplit_buffer_bytes(int(world), int(batch), int(heads))
+    if n == 0:
+        raise MlaError(1, last_error())
+    return int(n)
+
+
+def ipc_export(ptr) -> tuple[bytes, int]:
+    """CUDA IPC handle (64 bytes) of the allocation holding device pointer ``ptr``, and
+    ``ptr``'s offset in it."""
+    h = (ctypes.c_char * 64)()
+    off = ctypes.c_uint64()
+    check(load().mla_ipc_export(ptr, h, ctypes.byref(off)))
+    return bytes(h), int(off.value)
+
+
+def ipc_import(handle: bytes, offset: int) -> int:
+    """Device pointer, in this process, of a peer's memory exported by ``ipc_export``."""
+    h = (ctypes.c_char * 64).from_buffer_copy(handle)
+    p = ctypes.c_void_p()
+    check(load().mla_ipc_import(h, int(offset), ctypes.byref(p)))
+    return int(p.value)
+
+
+def ipc_close(ptr, offset) -> None:
+    check(load().mla_ipc_close(ptr, int(offset)))
+
+
+def seqsplit_exchange(bufs, world, rank, epoch, batch, heads, stream) -> None:
+    arr = (ctypes.c_void_p * len(bufs))(*bufs)
+    check(load().mla_seqsplit_exchange(arr, int(world), int(rank), int(epoch), int(batch), int(heads), stream))

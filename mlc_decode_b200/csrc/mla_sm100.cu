@@ -196,9 +196,9 @@ struct Cfg<Cv<T, kF16>> {
   static constexpr uint32_t kPvFmt = kToF16 ? 0u : Cfg<T>::kPvFmt;
   static constexpr uint32_t kRopeFmt = Cfg<T>::kFmt;
   static constexpr int kPParts = kToF16 ? 1 : Cfg<T>::kPParts;
-  static constexpr int kKStages = Cfg<T>::kKStages;
+  static constexpr int kKStages = kToF16 ? 5 : Cfg<T>::kKStages;
   static constexpr uint32_t kKStageBytes = kStageBytes;
-  static constexpr int kVStages = kToF16 ? 5 : Cfg<T>::kVStages;
+  static constexpr int kVStages = kToF16 ? 4 : Cfg<T>::kVStages;
   static constexpr int kV8Stages = 0;
   using PT = typename std::conditional<kToF16, __half, typename Cfg<T>::PT>::type;
 };

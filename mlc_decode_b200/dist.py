@@ -76,10 +76,16 @@ class SequenceSplitDecoder:
     """
 
     def __init__(self, batch: int, heads: int, seqlen_kv: int, group=None, cfg=None,
-                 partial_fn: Optional[PartialFn] = None, combine_fn: Optional[CombineFn] = None):
+                 partial_fn: Optional[PartialFn] = None, combine_fn: Optional[CombineFn] = None,
+                 exchange: str = "auto"):
+        if exchange not in ("auto", "p2p", "collective"):
+            raise ValueError(f"exchange must be 'auto', 'p2p' or 'collective', got {exchange!r}")
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.exchange = exchange
+        self._p2p = None      # (buffer, peer pointers, imports to close) once set up
+        self._epoch = 0       # calls made (the exchange's call number)
         self.batch, self.heads, self.seqlen_kv = int(batch), int(heads), int(seqlen_kv)
         self.start, self.end = seq_shard(self.seqlen_kv, self.rank, self.world)
         self.local_len = self.end - self.start
@@ -107,6 +113,78 @@ class SequenceSplitDecoder:
                                mine[b * h * DIM: b * h * (DIM + 1)].view(b, h))
         return self._bufs[key]
 
+    # -- the exchange over NVLink peer memory ---------------------------------
+    def _use_p2p(self, device) -> bool:
+        """Set up (once, collectively) the peer-memory exchange when every rank can use it:
+        CUDA kernels, an NCCL group of 2..8 ranks on one node with peer access."""
+        if self._p2p is not None:
+            return self._p2p is not False
+        ok = (self.exchange != "collective" and self._partial_is_kernel and device.type == "cuda"
+              and 2 <= self.world <= 8 and dist.get_backend(self.group) == "nccl")
+        if ok:
+            import socket
+
+            where = [None] * self.world
+            dist.all_gather_object(where, (socket.gethostname(), device.index), group=self.group)
+            ok = all(w[0] == where[0][0] for w in where) and all(
+                torch.cuda.can_device_access_peer(device.index, w[1]) for w in where if w[1] != device.index)
+        agree = [None] * self.world
+        dist.all_gather_object(agree, bool(ok), group=self.group)
+        if not all(agree):
+            if self.exchange == "p2p":
+                raise RuntimeError("exchange='p2p' needs every rank on one node with peer access")
+            self._p2p = False
+            return False
+        from . import capi
+
+        buf = torch.zeros(capi.seqsplit_buffer_bytes(self.world, self.batch, self.heads), dtype=torch.uint8,
+                          device=device)
+        handle = capi.ipc_export(buf.data_ptr())
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=self.group)
+        ptrs, opened = [], []
+        for r in range(self.world):
+            if r == self.rank:
+                ptrs.append(buf.data_ptr())
+            else:
+                p = capi.ipc_import(*handles[r])
+                ptrs.append(p)
+                opened.append((p, handles[r][1]))
+        self._p2p = (buf, ptrs, opened)
+        return True
+
+    def _p2p_views(self, par):
+        """(this rank's O and LSE block of parity par, every rank's O and LSE blocks of par)."""
+        buf = self._p2p[0]
+        b, h, w, ch = self.batch, self.heads, self.world, self._chunk()
+        f = buf[: 2 * w * ch * 4].view(torch.float32).view(2, w, ch)[par]
+        bh = b * h
+        mine = f[self.rank]
+        return (mine[: bh * DIM].view(b, h, DIM), mine[bh * DIM: bh * (DIM + 1)].view(b, h),
+                f[:, : bh * DIM].view(w, b, h, DIM), f[:, bh * DIM: bh * (DIM + 1)].view(w, b, h))
+
+    def exchange_status(self) -> int:
+        """Status word of the peer-memory exchange (0, or 0x201 when a wait for a peer gave up)."""
+        if not self._p2p:
+            return 0
+        buf = self._p2p[0]
+        hdr = buf.numel() - 256
+        return int(buf[hdr + 68: hdr + 72].view(torch.int32).item())
+
+    def close(self):
+        """Unmap the peers' buffers (peer-memory exchange)."""
+        if self._p2p:
+            from . import capi
+
+            for p, off in self._p2p[2]:
+                capi.ipc_close(p, off)
+            self._p2p = None
+
+    @property
+    def _partial_is_kernel(self) -> bool:
+        return self.kernel is not None or self.local_len == 0
+
+    # -- the call ---------------------------------------------------------------
     def __call__(self, q, q_pe, kv_part, k_pe_part, out, lse=None):
         self.local(q, q_pe, kv_part, k_pe_part)
         self.merge(out, lse, q.device)
@@ -120,7 +198,11 @@ class SequenceSplitDecoder:
         if kv_part.shape[1] != self.local_len or k_pe_part.shape[1] != self.local_len:
             raise ValueError(f"rank {self.rank} holds KV rows [{self.start}, {self.end}): "
                              f"expected {self.local_len} rows, got {kv_part.shape[1]}")
-        _, o, l = self._buffers(q.device)
+        self._epoch += 1
+        if self._use_p2p(q.device):
+            o, l, _, _ = self._p2p_views(self._epoch & 1)
+        else:
+            _, o, l = self._buffers(q.device)
         if self.local_len > 0:
             self._partial(q, q_pe, kv_part, k_pe_part, o, l)
         else:
@@ -129,10 +211,22 @@ class SequenceSplitDecoder:
             l.fill_(float("-inf"))
 
     def merge(self, out, lse=None, device=None):
-        """One all-gather of every rank's packed (O, LSE) block over the process group
-        (in place: this rank's block is the input), then the LSE merge into ``out``."""
+        """Every rank's (O, LSE) block into this rank's buffer, then the LSE merge into
+        ``out``: over NVLink peer memory (one launch stores this rank's block into every
+        peer's buffer and waits for theirs), or one in-place all-gather over the process
+        group; a collective either way, so every rank calls it."""
         b, h, w = self.batch, self.heads, self.world
-        buf, _, _ = self._buffers(device if device is not None else out.device)
+        dev = device if device is not None else out.device
+        if self._use_p2p(dev):
+            from . import capi
+
+            par = self._epoch & 1
+            _, _, o_all, l_all = self._p2p_views(par)
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            capi.seqsplit_exchange(self._p2p[1], w, self.rank, self._epoch, b, h, stream)
+            self._combine(l_all, o_all, out, lse)
+            return
+        buf, _, _ = self._buffers(dev)
         dist.all_gather_into_tensor(buf.view(-1), buf[self.rank], group=self.group)
         bh = b * h
         o_all = buf[:, : bh * DIM].view(w, b, h, DIM)

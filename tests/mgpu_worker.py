@@ -40,21 +40,28 @@ def main():
         res = O.check_parity(out.float().cpu().numpy(), lse.cpu().numpy(), ref, rl, "bf16")
         print(f"rank {rank} batch split {res}", flush=True)
         ok &= res["ok"]
-        # (b) sequence split
-        b, h, s = 1, 128, 20000
+        # (b) sequence split, both exchanges (over NVLink peer memory, and the NCCL
+        # all-gather), each called three times (both halves of the double buffer)
+        b, h, s = 2, 128, 20000
         inputs = O.make_inputs(b, h, s, "bf16", seed=72)
-        dec = SequenceSplitDecoder(b, h, s)
-        q, qp = inputs[0].to(dev), inputs[1].to(dev)
-        kv = inputs[2][:, dec.start:dec.end].contiguous().to(dev)
-        kp = inputs[3][:, dec.start:dec.end].contiguous().to(dev)
-        out = torch.empty(b, h, 512, dtype=torch.bfloat16, device=dev)
-        lse = torch.empty(b, h, device=dev)
-        dec(q, qp, kv, kp, out, lse)
-        torch.cuda.synchronize()
         ref, rl = O.ref_program_f64(*inputs)
-        res = O.check_parity(out.float().cpu().numpy(), lse.cpu().numpy(), ref, rl, "bf16")
-        print(f"rank {rank} sequence split rows [{dec.start}, {dec.end}) {res}", flush=True)
-        ok &= res["ok"]
+        for exchange in ("p2p", "collective"):
+            dec = SequenceSplitDecoder(b, h, s, exchange=exchange)
+            q, qp = inputs[0].to(dev), inputs[1].to(dev)
+            kv = inputs[2][:, dec.start:dec.end].contiguous().to(dev)
+            kp = inputs[3][:, dec.start:dec.end].contiguous().to(dev)
+            for call in range(3):
+                out = torch.full((b, h, 512), float("nan"), dtype=torch.bfloat16, device=dev)
+                lse = torch.full((b, h), float("nan"), device=dev)
+                dec(q, qp, kv, kp, out, lse)
+                torch.cuda.synchronize()
+                res = O.check_parity(out.float().cpu().numpy(), lse.cpu().numpy(), ref, rl, "bf16")
+                res["exchange_status"] = dec.exchange_status()
+                print(f"rank {rank} sequence split ({exchange}, call {call}) rows [{dec.start}, {dec.end}) {res}",
+                      flush=True)
+                ok &= res["ok"] and res["exchange_status"] == 0
+            dist.barrier()
+            dec.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -1,4 +1,5 @@
-"""Batch split and sequence split on 2 GPUs (NCCL), one process per GPU.
+"""Batch split and sequence split on 2 GPUs, one process per GPU: the sequence split
+with both exchanges (NVLink peer memory, NCCL all-gather).
 
 Skipped with fewer than two GPUs.  The ranks run tests/mgpu_worker.py under
 torch.distributed.run on 127.0.0.1; NVLS stays off (NCCL_NVLS_ENABLE=0).
@@ -31,4 +32,5 @@ def test_two_gpu_batch_and_sequence_split():
            os.path.join(HERE, "mgpu_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    assert r.stdout.count("'ok': True") == 4, r.stdout
+    # per rank: the batch split, then 3 calls of each sequence-split exchange
+    assert r.stdout.count("'ok': True") == 2 * (1 + 2 * 3), r.stdout
