@@ -343,3 +343,8 @@ def ipc_close(ptr, offset) -> None:
 def seqsplit_exchange(bufs, world, rank, epoch, batch, heads, stream) -> None:
     arr = (ctypes.c_void_p * len(bufs))(*bufs)
     check(load().mla_seqsplit_exchange(arr, int(world), int(rank), int(epoch), int(batch), int(heads), stream))
+
+
+def seqsplit_exchange_raw(arr, world, rank, epoch, batch, heads, stream) -> None:
+    """seqsplit_exchange with the buffers already as a ctypes c_void_p array."""
+    check(load().mla_seqsplit_exchange(arr, int(world), int(rank), int(epoch), int(batch), int(heads), stream))

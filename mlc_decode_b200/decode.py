@@ -176,15 +176,15 @@ class MlaDecodeKernel:
         if dtype not in _DTYPES:
             raise ValueError(f"q must be float16 or bfloat16, got {dtype}")
         dev = q.device
-        _check_tensor("q", q, (b, h, DIM), dtype, None)
-        _check_tensor("q_pe", q_pe, (b, h, PE_DIM), dtype, dev)
-        _check_tensor("kv", kv, (b, s, 1, DIM), dtype, dev)
-        _check_tensor("k_pe", k_pe, (b, s, 1, PE_DIM), dtype, dev)
-        _check_tensor("o", o, (b, h, DIM), torch.float32, dev)
-        _check_tensor("lse", lse, (b, h), torch.float32, dev)
+        shapes = self._shapes
+        for name, t, shape, dt in (("q", q, shapes[0], dtype), ("q_pe", q_pe, shapes[1], dtype),
+                                   ("kv", kv, shapes[2], dtype), ("k_pe", k_pe, shapes[3], dtype),
+                                   ("o", o, shapes[0], torch.float32), ("lse", lse, shapes[0][:2], torch.float32)):
+            if not (type(t) is torch.Tensor and t.dtype == dt and t.device == dev and t.shape == shape
+                    and t.is_contiguous() and dev.type == "cuda"):
+                _check_tensor(name, t, shape, dt, dev)
         ws = self._workspace(dev, dtype)
-        with torch.cuda.device(dev):
-            stream = torch.cuda.current_stream(dev).cuda_stream
+        stream = torch.cuda.current_stream(dev).cuda_stream
         capi.decode_partial(q.data_ptr(), q_pe.data_ptr(), kv.data_ptr(), k_pe.data_ptr(), o.data_ptr(),
                             lse.data_ptr(), ws.data_ptr(), ws.numel(), b, h, s, _DTYPES[dtype],
                             self._ccfg, stream)

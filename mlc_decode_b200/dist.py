@@ -24,7 +24,11 @@ from typing import Callable, Optional
 import torch
 import torch.distributed as dist
 
+from . import capi as _capi
 from .decode import DIM, MlaDecodeKernel, combine
+
+_OUT_TYPES = {torch.float16: _capi.MLA_DTYPE_F16, torch.bfloat16: _capi.MLA_DTYPE_BF16,
+              torch.float32: _capi.MLA_DTYPE_F32}
 
 TILE = 128   # KV rows per tile of the tensor-core kernel: part boundaries fall on tiles
 
@@ -150,18 +154,25 @@ class SequenceSplitDecoder:
                 p = capi.ipc_import(*handles[r])
                 ptrs.append(p)
                 opened.append((p, handles[r][1]))
-        self._p2p = (buf, ptrs, opened)
+        import ctypes
+
+        # views and pointers made once: a decode step runs this every call
+        b, h, w, ch = self.batch, self.heads, self.world, self._chunk()
+        bh = b * h
+        views = []
+        for par in range(2):
+            f = buf[: 2 * w * ch * 4].view(torch.float32).view(2, w, ch)[par]
+            mine = f[self.rank]
+            views.append((mine[: bh * DIM].view(b, h, DIM), mine[bh * DIM: bh * (DIM + 1)].view(b, h),
+                          f[:, : bh * DIM].view(w, b, h, DIM), f[:, bh * DIM: bh * (DIM + 1)].view(w, b, h),
+                          f.data_ptr(), f.data_ptr() + bh * DIM * 4))
+        self._p2p = (buf, ptrs, opened, views, (ctypes.c_void_p * w)(*ptrs))
         return True
 
     def _p2p_views(self, par):
-        """(this rank's O and LSE block of parity par, every rank's O and LSE blocks of par)."""
-        buf = self._p2p[0]
-        b, h, w, ch = self.batch, self.heads, self.world, self._chunk()
-        f = buf[: 2 * w * ch * 4].view(torch.float32).view(2, w, ch)[par]
-        bh = b * h
-        mine = f[self.rank]
-        return (mine[: bh * DIM].view(b, h, DIM), mine[bh * DIM: bh * (DIM + 1)].view(b, h),
-                f[:, : bh * DIM].view(w, b, h, DIM), f[:, bh * DIM: bh * (DIM + 1)].view(w, b, h))
+        """(this rank's O and LSE block of parity par, every rank's O and LSE blocks of par,
+        and the device addresses of the blocks' O and LSE rows)."""
+        return self._p2p[3][par]
 
     def exchange_status(self) -> int:
         """Status word of the peer-memory exchange (0, or 0x201 when a wait for a peer gave up)."""
@@ -179,6 +190,13 @@ class SequenceSplitDecoder:
             for p, off in self._p2p[2]:
                 capi.ipc_close(p, off)
             self._p2p = None
+
+    def _out_ok(self, out, lse, dev) -> bool:
+        b, h = self.batch, self.heads
+        return (type(out) is torch.Tensor and out.dtype in _OUT_TYPES and out.device == dev
+                and out.shape == (b, h, DIM) and out.is_contiguous()
+                and (lse is None or (lse.dtype == torch.float32 and lse.device == dev and lse.shape == (b, h)
+                                     and lse.is_contiguous())))
 
     @property
     def _partial_is_kernel(self) -> bool:
@@ -200,7 +218,7 @@ class SequenceSplitDecoder:
                              f"expected {self.local_len} rows, got {kv_part.shape[1]}")
         self._epoch += 1
         if self._use_p2p(q.device):
-            o, l, _, _ = self._p2p_views(self._epoch & 1)
+            o, l = self._p2p_views(self._epoch & 1)[:2]
         else:
             _, o, l = self._buffers(q.device)
         if self.local_len > 0:
@@ -221,14 +239,25 @@ class SequenceSplitDecoder:
             from . import capi
 
             par = self._epoch & 1
-            _, _, o_all, l_all = self._p2p_views(par)
+            _, _, o_all, l_all, o_ptr, l_ptr = self._p2p_views(par)
             stream = torch.cuda.current_stream(dev).cuda_stream
-            capi.seqsplit_exchange(self._p2p[1], w, self.rank, self._epoch, b, h, stream)
-            self._combine(l_all, o_all, out, lse)
+            capi.seqsplit_exchange_raw(self._p2p[4], w, self.rank, self._epoch, b, h, stream)
+            if self._combine is combine and self._out_ok(out, lse, dev):
+                # the blocks' layout was checked when the views were made
+                capi.combine_strided(l_ptr, self._chunk(), o_ptr, self._chunk(), w, b, h, out.data_ptr(),
+                                     None if lse is None else lse.data_ptr(), _OUT_TYPES[out.dtype], stream)
+            else:
+                self._combine(l_all, o_all, out, lse)
             return
         buf, _, _ = self._buffers(dev)
         dist.all_gather_into_tensor(buf.view(-1), buf[self.rank], group=self.group)
         bh = b * h
+        if self._combine is combine and dev.type == "cuda" and self._out_ok(out, lse, dev):
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            _capi.combine_strided(buf.data_ptr() + bh * DIM * 4, self._chunk(), buf.data_ptr(), self._chunk(), w, b,
+                                  h, out.data_ptr(), None if lse is None else lse.data_ptr(), _OUT_TYPES[out.dtype],
+                                  stream)
+            return
         o_all = buf[:, : bh * DIM].view(w, b, h, DIM)
         l_all = buf[:, bh * DIM: bh * (DIM + 1)].view(w, b, h)
         self._combine(l_all, o_all, out, lse)
