@@ -1138,17 +1138,24 @@ __device__ __forceinline__ float quantize_q(const Params& p, int v, uint32_t ran
   const uint4* rg = reinterpret_cast<const uint4*>(p.qpe) + row * (kPeDim / 8);
   const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
   float amax = 0.f, rmax = 0.f;
+  // eight 16-byte loads of the row in flight at a time (one at a time, the scan
+  // took ~64 L2 round trips before the piece's first QK^T could start)
 #pragma unroll 1
-  for (int g = 0; g < kDim / 8; ++g) {
-    const uint4 x = real ? __ldg(qg + g) : zero;
-    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+  for (int g0 = 0; g0 < kDim / 8; g0 += 8) {
+    uint4 xs[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = Elt<Out>::to2(w[e]);
-      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    for (int k = 0; k < 8; ++k) xs[k] = real ? __ldg(qg + g0 + k) : zero;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t w[4] = {xs[k].x, xs[k].y, xs[k].z, xs[k].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = Elt<Out>::to2(w[e]);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
     }
   }
-#pragma unroll 1
+#pragma unroll
   for (int g = 0; g < kPeDim / 8; ++g) {
     const uint4 x = real ? __ldg(rg + g) : zero;
     const uint32_t w[4] = {x.x, x.y, x.z, x.w};
@@ -1899,6 +1906,9 @@ mla_sm100_decode_kernel(const __grid_constant__ Params p) {
   ptx::cluster_sync();
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  // a combine launch queued behind this grid may be set up now (it waits for this
+  // grid's completion before it reads anything)
+  if (threadIdx.x == 0) ptx::grid_dep_launch();
   // clock probe: SM cycles and %globaltimer ns of this CTA's run (thread 0 of CTA 0)
   const bool probe = blockIdx.x == 0 && threadIdx.x == 0 && p.status != nullptr;
   const uint64_t probe_c0 = probe ? (uint64_t)clock64() : 0ull;
@@ -2010,10 +2020,14 @@ mla_wait_selftest_kernel(uint32_t* status, unsigned long long* result, uint64_t 
 // ---------------------------------------------------------------------------
 // combine launch for sequences split between more pairs than the kernel above
 // merges itself (fuse_max): one CTA per (head, sequence) of kCombineGroups groups of
-// 128 threads; group g takes every kCombineGroups-th piece, 4 columns per thread and
-// eight pieces in flight per round, and the groups' sums meet in shared memory.
-// Other sequences were written by the decode kernel and are skipped.  Same LSE
-// algebra as mla_combine.cu (mla_decode.py:212-246).
+// 128 threads; group g takes every kCombineGroups-th piece and thread t columns
+// [4t, 4t + 4).  Latency, not bandwidth, bounds it (a few MB, just written, in L2):
+// every thread issues the loads of all its pieces (up to kCombinePer) at once,
+// before it needs the LSEs, so that one round trip covers the whole merge; the
+// groups' sums meet in shared memory.  Launched as a programmatic dependent of the
+// decode kernel: the grid is set up while the decode kernel runs, and waits for its
+// completion before the first load.  Sequences the decode kernel wrote itself are
+// skipped.  Same LSE algebra as mla_combine.cu (mla_decode.py:212-246).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void store4_out(float* dst, float4 v) { *reinterpret_cast<float4*>(dst) = v; }
 template <typename T>
@@ -2022,6 +2036,7 @@ __device__ __forceinline__ void store4_out(T* dst, float4 v) {
 }
 
 constexpr int kCombineGroups = 4;
+constexpr int kCombinePer = 20;   // pieces per thread and round: 80 per round (B200: at most 74)
 
 template <typename OutT>
 __global__ void __launch_bounds__(128 * kCombineGroups)
@@ -2029,11 +2044,12 @@ mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restr
                         OutT* __restrict__ out, float* __restrict__ lse_out, const uint32_t* cu,
                         uint32_t total_fixed, int nt, int pairs, int vbatch, int heads, int hgroups,
                         int fuse_max) {
+  constexpr int G = kCombineGroups;
   __shared__ float s_lse[kMaxPairs];
-  __shared__ uint32_t s_slot[kMaxPairs];
-  __shared__ float4 s_acc[kCombineGroups - 1][128];
+  __shared__ float4 s_acc[G - 1][128];
   const int head = blockIdx.x, bb = blockIdx.y;
   const int grp = threadIdx.x >> 7, tid = threadIdx.x & 127;   // piece group, column quad
+  ptx::grid_dep_wait();   // the decode kernel's partials are complete and visible
   TileMap m;
   m.cu = cu;
   m.nt = (uint32_t)nt;
@@ -2045,38 +2061,52 @@ mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restr
   pairs_of_sequence(m, bb, &pf, &pl);
   const int n = pl - pf + 1;
   if (n <= fuse_max) return;   // whole, or merged by the decode kernel
-  for (int k = threadIdx.x; k < n; k += 128 * kCombineGroups) {
-    const uint32_t sl = (uint32_t)pair_slot(m, pf + k, bb);
-    s_slot[k] = sl;
-    s_lse[k] = __ldg(part_lse + (size_t)sl * kHeads + head);
+  // piece k's slot (pair_slot without a division per piece): every pair after the
+  // first starts its range inside the sequence, so the piece is that pair's first
+  const size_t slot0 = pair_slot(m, pf, bb);
+  auto slot = [&](int k) -> size_t { return k == 0 ? slot0 : (size_t)(pf + k) * 2; };
+  const float4* po = reinterpret_cast<const float4*>(part_o) + (size_t)head * (kDim / 4) + tid;
+  constexpr size_t kSlotQuads = (size_t)kHeads * kDim / 4;   // float4 per slot
+  // first round of O loads in flight before anything waits
+  float4 v[kCombinePer];
+#pragma unroll
+  for (int u = 0; u < kCombinePer; ++u) {
+    const int k = grp + G * u;
+    v[u] = k < n ? __ldcg(po + slot(k) * kSlotQuads) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  for (int k = threadIdx.x; k < n; k += 128 * G) s_lse[k] = __ldcg(part_lse + slot(k) * kHeads + head);
   __syncthreads();
+  // the sequence's LSE: every warp reduces the n piece LSEs itself (lanes over pieces)
+  const int lane = threadIdx.x & 31;
   float mx = -INFINITY;
-  for (int k = 0; k < n; ++k) mx = fmaxf(mx, s_lse[k]);
+  for (int k = lane; k < n; k += 32) mx = fmaxf(mx, s_lse[k]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float sum = 0.f;
-  for (int k = 0; k < n; ++k) sum += exp2f((s_lse[k] - mx) * kLog2e);
-  const float lse = mx + logf(sum);
+  if (mx != -INFINITY)
+    for (int k = lane; k < n; k += 32) sum += exp2f((s_lse[k] - mx) * kLog2e);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float lse = mx != -INFINITY ? mx + logf(sum) : -INFINITY;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  // pieces grp, grp + G, grp + 2G, ...: eight partial rows in flight per thread and
-  // round (the tail rides in the last round)
-  constexpr int G = kCombineGroups;
-  for (int k0 = grp; k0 < n; k0 += 8 * G) {
-    float4 v[8];
+  for (int k0 = 0;; k0 += G * kCombinePer) {
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int k = k0 + u * G;
-      v[u] = k < n ? __ldg(reinterpret_cast<const float4*>(part_o + ((size_t)s_slot[k] * kHeads + head) * kDim) + tid)
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int k = k0 + u * G;
+    for (int u = 0; u < kCombinePer; ++u) {
+      const int k = k0 + grp + G * u;
       if (k >= n) break;
-      const float w = exp2f((s_lse[k] - lse) * kLog2e);
+      const float w = lse != -INFINITY ? exp2f((s_lse[k] - lse) * kLog2e) : 0.f;
       acc.x = fmaf(w, v[u].x, acc.x);
       acc.y = fmaf(w, v[u].y, acc.y);
       acc.z = fmaf(w, v[u].z, acc.z);
       acc.w = fmaf(w, v[u].w, acc.w);
+    }
+    const int k1 = k0 + G * kCombinePer;
+    if (k1 >= n) break;
+    // more pieces than one round holds (more pairs than a B200 has)
+#pragma unroll
+    for (int u = 0; u < kCombinePer; ++u) {
+      const int k = k1 + grp + G * u;
+      v[u] = k < n ? __ldcg(po + slot(k) * kSlotQuads) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
   if (grp > 0) s_acc[grp - 1][tid] = acc;
@@ -2552,20 +2582,29 @@ cudaError_t launch_sm100_combine(const DecodeArgs& a) {
   const QShape qs = qshape(a);
   const int hg = qs.hg, vb = qs.vb;
   const uint32_t total = (uint32_t)vb * (uint32_t)nt;
-  const dim3 grid(kHeads, vb);
+  // a programmatic dependent of the decode kernel before it in the stream
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(kHeads, vb, 1);
+  cfg.blockDim = dim3(128 * kCombineGroups, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const float* pl = a.part_lse;
+  const float* po = a.part_o;
+  const uint32_t* cu = a.cu_tiles;
+  const int pairs = a.plan.bpc, g = qs.g, fm = kFuseMaxPieces;
   if (a.out_dtype == MLA_DTYPE_F32)
-    mla_pair_combine_kernel<float><<<grid, 128 * kCombineGroups, 0, a.stream>>>(
-        a.part_lse, a.part_o, static_cast<float*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb, qs.g,
-        hg, kFuseMaxPieces);
-  else if (a.dtype == MLA_DTYPE_BF16)
-    mla_pair_combine_kernel<__nv_bfloat16><<<grid, 128 * kCombineGroups, 0, a.stream>>>(
-        a.part_lse, a.part_o, static_cast<__nv_bfloat16*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb,
-        qs.g, hg, kFuseMaxPieces);
-  else
-    mla_pair_combine_kernel<__half><<<grid, 128 * kCombineGroups, 0, a.stream>>>(
-        a.part_lse, a.part_o, static_cast<__half*>(a.out), a.lse, a.cu_tiles, total, nt, a.plan.bpc, vb, qs.g,
-        hg, kFuseMaxPieces);
-  return cudaGetLastError();
+    return cudaLaunchKernelEx(&cfg, mla_pair_combine_kernel<float>, pl, po, static_cast<float*>(a.out), a.lse, cu,
+                              total, nt, pairs, vb, g, hg, fm);
+  if (a.dtype == MLA_DTYPE_BF16)
+    return cudaLaunchKernelEx(&cfg, mla_pair_combine_kernel<__nv_bfloat16>, pl, po,
+                              static_cast<__nv_bfloat16*>(a.out), a.lse, cu, total, nt, pairs, vb, g, hg, fm);
+  return cudaLaunchKernelEx(&cfg, mla_pair_combine_kernel<__half>, pl, po, static_cast<__half*>(a.out), a.lse, cu,
+                            total, nt, pairs, vb, g, hg, fm);
 }
 
 }  // namespace mla

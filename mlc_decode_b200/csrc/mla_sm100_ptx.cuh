@@ -357,5 +357,13 @@ __host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_fmt, uint32_t m, ui
          | ((m >> 4) << 24);       // M
 }
 
+// Programmatic dependent launch.  A grid launched with the attribute
+// cudaLaunchAttributeProgrammaticStreamSerialization may start once every CTA of
+// the grid before it in the stream has called launch_dependents (or exited);
+// grid_dep_wait() then blocks until that grid has completed and its memory
+// operations are visible.  Both are no-ops in a grid launched without it.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace ptx
 }  // namespace mla
