@@ -111,8 +111,10 @@ def workload_name(a):
         name += ", FP8 (e4m3) latent KV cache"
     if a.seq_split:
         name = f"mla_decode b{a.batch} h{a.heads} s{a.kv_ctx} {a.dtype} (dim 512+64, kv_heads 1), "
-        how = {"collective": "all-gathered over NCCL", "p2p": "pushed over NVLink peer memory",
-               "auto": "exchanged over NVLink peer memory (NCCL all-gather where peers are not reachable)"}
+        how = {"collective": "all-gathered over NCCL",
+               "p2p": "merged per GPU and pushed row by row over NVLink peer memory",
+               "auto": "merged per GPU and pushed row by row over NVLink peer memory (NCCL all-gather where "
+                       "peers are not reachable)"}
         name += (f"KV rows split across {a.gpus} GPU(s), (O, LSE) {how[a.seq_exchange]} and merged"
                  if a.gpus > 1 else "whole sequence on one GPU (the sequence split's 1-GPU point)")
     return name
@@ -381,18 +383,22 @@ def run_ours(a, rank, world, local_rank):
         k_pe = torch.randn(b, dec.local_len, 1, 64, device=dev, generator=g).to(tdt)
 
         class _Seq:
+            # A timed step is the whole call: over NVLink peer memory two launches
+            # (this rank's decode, then one launch that merges its rows, stores them
+            # into the peers' buffers and merges theirs); over the all-gather the
+            # decode and its combine, the collective and the merge.
             def __call__(self, q_, qp_, kv_, kp_, out_):
                 dec(q_, qp_, kv_, kp_, out_)
 
-            def splitkv(self, q_, qp_, kv_, kp_, out_):
-                dec.local(q_, qp_, kv_, kp_)       # this rank's partial decode
+            splitkv = __call__
 
             def combine_ws(self, out_):
-                dec.merge(out_)                    # exchange of (O, LSE) blocks + merge
+                pass
 
         kern = _Seq()
         probe_obj = dec.kernel
-        launches = (dec.kernel.launches_per_call(tdt) if dec.kernel is not None else 0) + 1
+        p2p = dec._use_p2p(dev)
+        launches = 2 if p2p else (dec.kernel.launches_per_call(tdt) if dec.kernel is not None else 0) + 1
     else:
         kern = MlaDecodeKernel(b, h, 1, s, cfg=cfg)
         probe_obj = kern
@@ -451,6 +457,11 @@ def run_ours(a, rank, world, local_rank):
     total_ms, dec_mean_ms = float(t[0]), float(t[1])
     us_call = total_ms * 1000.0 / K
     dec_us = dec_mean_ms * 1000.0
+    if a.seq_split and world > 1:
+        # the dominant kernel's time, for the roofline: this rank's decode launch alone
+        # (the same decode kernel the call launches first), timed after the timed
+        # region with the same flush before each launch
+        dec_us = seq_decode_us(dec, q, q_pe, kv, k_pe, out, flush, min(K, 50), dev, world)
 
     # ---- e2e through the public API with host buffers ------------------------
     hq, hqp, hkv, hkp = (x.cpu().pin_memory() for x in (q, q_pe, kv, k_pe))
@@ -528,7 +539,8 @@ def run_ours(a, rank, world, local_rank):
                      "traffic": None if (a.paged or a.fp8 or a.seq_split) else traffic_from_profiles(a),
                      "kernel": ("paged decode call (plan + decode + combine)" if a.paged else
                                 "FP8-KV split-KV decode kernel" if a.fp8 else
-                                "partial decode of this GPU's KV rows" if a.seq_split and world > 1 else
+                                "decode kernel of this GPU's KV rows (the first of the call's launches)"
+                                if a.seq_split and world > 1 else
                                 "split-KV decode kernel"),
                      "kernel_us": round(dec_us, 3), "peak_source": peaks["source"],
                      "kernel_clock": kclk,
@@ -554,6 +566,30 @@ def run_ours(a, rank, world, local_rank):
                                 "sample": f"{bs} of {b} sequences, median of {len(times)} runs, "
                                           f"scaled x{b / bs:g} to the full call"}
     print(json.dumps(line), flush=True)
+
+
+def seq_decode_us(dec, q, q_pe, kv, k_pe, out, flush, n, dev, world):
+    """Mean device time of the sequence split's decode launch on this rank's KV rows
+    (MlaDecodeKernel.splitkv: the decode kernel alone), max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    k = dec.kernel
+    if k is None:
+        return 0.0
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    for i in range(n):
+        if flush is not None:
+            flush.fill_(i & 0xFF)
+        ev[i][0].record()
+        k.splitkv(q, q_pe, kv, k_pe, out)
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    t = torch.tensor([statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev) * 1000.0], device=dev,
+                     dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0])
 
 
 def main():

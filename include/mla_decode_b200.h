@@ -182,7 +182,8 @@ int32_t mla_combine_strided(const float* part_lse, int64_t lse_split_stride,
 
 /*
  * The sequence split's exchange over NVLink, without a collective library (no
- * reference counterpart: the reference has no multi-GPU path).  world (2..8)
+ * reference counterpart: the reference has no multi-GPU path).  world (2..8; 1..8
+ * for mla_seqsplit_decode / mla_seqsplit_merge below)
  * ranks, one GPU each on one node, each own a gather buffer of
  * mla_seqsplit_buffer_bytes(world, batch, heads) bytes (256-byte aligned, zeroed
  * once) and map every peer's buffer with mla_ipc_export / mla_ipc_import (CUDA
@@ -190,7 +191,9 @@ int32_t mla_combine_strided(const float* part_lse, int64_t lse_split_stride,
  * a buffer: float blocks [2][world][chunk] with chunk = batch*heads*512 +
  * round_up(batch*heads, 64): block [epoch & 1][r] is rank r's (O, LSE) of call
  * `epoch` (O rows, then the LSEs); then a 256-byte header (flags, a counter, the
- * status word at byte 68: 0, or 0x201 when a wait gave up).
+ * status word at byte 68: 0, or 0x201 when a wait gave up), then row words
+ * uint32 pairs [2][world][round_up(batch*heads, 64)][512] and LSE words uint32
+ * pairs [2][world][round_up(batch*heads, 64)] (value bits, call number).
  * For call `epoch` (1, 2, 3, ... the same on every rank), rank `rank` writes its
  * block [epoch & 1][rank] in its own buffer (mla_decode_partial into it), then
  * mla_seqsplit_exchange enqueues one launch that stores that block into every
@@ -206,6 +209,31 @@ int32_t mla_ipc_import(const void* handle /* 64 bytes */, uint64_t offset, void*
 int32_t mla_ipc_close(void* ptr, uint64_t offset);
 int32_t mla_seqsplit_exchange(void* const* bufs, int32_t world, int32_t rank, uint32_t epoch,
                               int32_t batch, int32_t heads, void* stream);
+
+/*
+ * The sequence split in two launches per call (same buffers, IPC mapping and
+ * call numbering as above; world 1..8, world 1 needing no peers).  Rank `rank`
+ * decodes q against its rows [0, seqlen_part) of every sequence (kv_part /
+ * k_pe_part, the layout of mla_decode_fwd; same workspace and checks) to float32
+ * (O, LSE) in its block [epoch & 1][rank]; then one launch merges that result
+ * row by row (straight from the decode kernel's pieces when a sequence was split
+ * between many CTA pairs), stores each merged row into every peer's row words
+ * over NVLink (each value paired with the call number, so no fence or flag is
+ * needed), polls (at most 2 s, status word as above) until every peer's words
+ * carry this call's number, and writes the LSE merge over all ranks to out
+ * ([batch, heads, 512], dtype) and lse (float32 [batch, heads], optional).  Every
+ * rank must make the call.  mla_seqsplit_merge is the second launch alone, for a
+ * rank whose block [epoch & 1][rank] is already written (mla_decode_partial into
+ * it, or O = 0 and LSE = -inf for a rank with no rows); out may be float32 there
+ * (dtype 2).
+ */
+int32_t mla_seqsplit_decode(const void* q, const void* q_pe, const void* kv_part, const void* k_pe_part,
+                            void* out, float* lse, void* workspace, size_t workspace_bytes,
+                            int32_t batch, int32_t heads, int32_t seqlen_part, int32_t dtype,
+                            void* const* bufs, int32_t world, int32_t rank, uint32_t epoch,
+                            const MlaCfg* cfg, void* stream);
+int32_t mla_seqsplit_merge(void* const* bufs, int32_t world, int32_t rank, uint32_t epoch, int32_t batch,
+                           int32_t heads, void* out, float* lse, int32_t dtype, void* stream);
 
 /*
  * mla_decode_fwd for one contiguous part of every sequence's KV cache, with a

@@ -30,7 +30,7 @@ EXPORTED_SYMBOLS = ("mla_abi_version", "mla_last_error", "mla_split_plan",
                     "mla_decode_fp8kv", "mla_decode_ext_fp8kv", "mla_selftest_wait_timeout",
                     "mla_noalloc_init", "mla_noalloc_status", "mla_combine_strided",
                     "mla_seqsplit_buffer_bytes", "mla_ipc_export", "mla_ipc_import", "mla_ipc_close",
-                    "mla_seqsplit_exchange")
+                    "mla_seqsplit_exchange", "mla_seqsplit_decode", "mla_seqsplit_merge")
 
 MLA_SELFTEST_STATUS = 0x1FF   # status word written by mla_selftest_wait_timeout
 
@@ -138,6 +138,12 @@ def load(build_if_missing: bool = True):
         lib.mla_seqsplit_exchange.argtypes = [ctypes.POINTER(ctypes.c_void_p), i32, i32, ctypes.c_uint32, i32, i32,
                                               vp]
         lib.mla_seqsplit_exchange.restype = i32
+        pvp = ctypes.POINTER(ctypes.c_void_p)
+        lib.mla_seqsplit_decode.argtypes = [vp, vp, vp, vp, vp, vp, vp, sz, i32, i32, i32, i32, pvp, i32, i32,
+                                            ctypes.c_uint32, ctypes.POINTER(MlaCfg), vp]
+        lib.mla_seqsplit_decode.restype = i32
+        lib.mla_seqsplit_merge.argtypes = [pvp, i32, i32, ctypes.c_uint32, i32, i32, vp, vp, i32, vp]
+        lib.mla_seqsplit_merge.restype = i32
         _lib = lib
         return lib
 
@@ -348,3 +354,22 @@ def seqsplit_exchange(bufs, world, rank, epoch, batch, heads, stream) -> None:
 def seqsplit_exchange_raw(arr, world, rank, epoch, batch, heads, stream) -> None:
     """seqsplit_exchange with the buffers already as a ctypes c_void_p array."""
     check(load().mla_seqsplit_exchange(arr, int(world), int(rank), int(epoch), int(batch), int(heads), stream))
+
+
+def seqsplit_decode(q, q_pe, kv_part, k_pe_part, out, lse, ws, ws_bytes, batch, heads, seqlen_part, dtype, bufs,
+                    world, rank, epoch, cfg: MlaCfg, stream) -> None:
+    """mla_seqsplit_decode: this rank's decode, then the row-wise exchange and merge.
+
+    ``bufs``: every rank's gather buffer pointer, a sequence or a ctypes c_void_p array.
+    """
+    arr = bufs if isinstance(bufs, ctypes.Array) else (ctypes.c_void_p * len(bufs))(*bufs)
+    check(load().mla_seqsplit_decode(q, q_pe, kv_part, k_pe_part, out, lse, ws, ws_bytes, int(batch), int(heads),
+                                     int(seqlen_part), int(dtype), arr, int(world), int(rank), int(epoch),
+                                     ctypes.byref(cfg), stream))
+
+
+def seqsplit_merge(bufs, world, rank, epoch, batch, heads, out, lse, dtype, stream) -> None:
+    """mla_seqsplit_merge: the row-wise exchange and merge of blocks already written."""
+    arr = bufs if isinstance(bufs, ctypes.Array) else (ctypes.c_void_p * len(bufs))(*bufs)
+    check(load().mla_seqsplit_merge(arr, int(world), int(rank), int(epoch), int(batch), int(heads), out, lse,
+                                    int(dtype), stream))

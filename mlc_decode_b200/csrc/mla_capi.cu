@@ -370,6 +370,101 @@ int32_t mla_decode_partial(const void* q, const void* q_pe, const void* kv, cons
   return run_combine_ws("mla_decode_partial", a, r);
 }
 
+// The sequence split's gather buffers of a call: checks and the PeerRows view.
+static int seqsplit_view(const char* fn, void* const* bufs, int32_t world, int32_t rank, uint32_t epoch,
+                         int32_t batch, int32_t heads, PeerRows* x) {
+  if (bufs == nullptr || world < 1 || world > kSeqMaxWorld || rank < 0 || rank >= world || epoch == 0 ||
+      batch < 1 || heads < 1) {
+    set_error("%s: bad argument (world %d, rank %d, epoch %u, batch %d, heads %d)", fn, world, rank, epoch, batch,
+              heads);
+    return MLA_ERR_ARG;
+  }
+  *x = PeerRows{};
+  for (int q = 0; q < world; ++q) {
+    if (bufs[q] == nullptr || (reinterpret_cast<uintptr_t>(bufs[q]) & 255u) != 0) {
+      set_error("%s: buffer %d is null or not 256-byte aligned", fn, q);
+      return MLA_ERR_ARG;
+    }
+    x->bufs[q] = static_cast<float*>(bufs[q]);
+  }
+  x->chunk = seq_chunk_floats(batch, heads);
+  x->header = seq_header_offset(world, batch, heads);
+  x->ll_rows = seq_ll_rows_offset(world, batch, heads);
+  x->ll_lse = seq_ll_lse_offset(world, batch, heads);
+  x->rows_pad = seq_rows_pad(batch, heads);
+  x->world = world;
+  x->rank = rank;
+  x->par = (int)(epoch & 1u);
+  x->epoch = epoch;
+  return MLA_OK;
+}
+
+int32_t mla_seqsplit_decode(const void* q, const void* q_pe, const void* kv_part, const void* k_pe_part, void* out,
+                            float* lse, void* workspace, size_t workspace_bytes, int32_t batch, int32_t heads,
+                            int32_t seqlen_part, int32_t dtype, void* const* bufs, int32_t world, int32_t rank,
+                            uint32_t epoch, const MlaCfg* cfg, void* stream) {
+  const char* fn = "mla_seqsplit_decode";
+  PeerRows x;
+  int rc = seqsplit_view(fn, bufs, world, rank, epoch, batch, heads, &x);
+  if (rc != MLA_OK) return rc;
+  if (out == nullptr || !aligned16(out)) {
+    set_error("%s: out is null or not 16-byte aligned", fn);
+    return MLA_ERR_ARG;
+  }
+  // this rank's part decodes to float32 (O, LSE) in its own block of its own buffer
+  float* own = x.bufs[rank] + ((size_t)x.par * world + rank) * x.chunk;
+  float* own_lse = own + (size_t)batch * heads * kDim;
+  DecodeArgs a;
+  Resolved r;
+  size_t need = 0;
+  rc = prepare(fn, q, q_pe, kv_part, k_pe_part, own, own_lse, workspace, workspace_bytes, batch, heads, seqlen_part,
+               dtype, cfg, stream, true, &a, &r, &need);
+  if (rc != MLA_OK) return rc;
+  a.out_dtype = MLA_DTYPE_F32;
+  rc = run_splitkv(fn, a, r);
+  if (rc != MLA_OK) return rc;
+  // sequences split between many CTA pairs are merged from their pieces inside the
+  // exchange launch; anything else is already in the block
+  const bool pieces = r.kernel == MLA_KERNEL_TC && r.plan.needs_combine && r.tc_variant == 1;
+  if (!pieces) {
+    rc = run_combine_ws(fn, a, r);
+    if (rc != MLA_OK) return rc;
+  }
+  const cudaError_t err = launch_seqsplit_combine(a, pieces, x, out, lse, dtype);
+  if (err != cudaSuccess) {
+    set_error("%s: exchange launch failed: %s", fn, cudaGetErrorString(err));
+    return MLA_ERR_CUDA;
+  }
+  return MLA_OK;
+}
+
+int32_t mla_seqsplit_merge(void* const* bufs, int32_t world, int32_t rank, uint32_t epoch, int32_t batch,
+                           int32_t heads, void* out, float* lse, int32_t dtype, void* stream) {
+  const char* fn = "mla_seqsplit_merge";
+  PeerRows x;
+  int rc = seqsplit_view(fn, bufs, world, rank, epoch, batch, heads, &x);
+  if (rc != MLA_OK) return rc;
+  if (out == nullptr || !aligned16(out)) {
+    set_error("%s: out is null or not 16-byte aligned", fn);
+    return MLA_ERR_ARG;
+  }
+  if (dtype != MLA_DTYPE_F16 && dtype != MLA_DTYPE_BF16 && dtype != MLA_DTYPE_F32) {
+    set_error("%s: dtype must be 0, 1 or 2", fn);
+    return MLA_ERR_ARG;
+  }
+  DecodeArgs a{};
+  a.batch = batch;
+  a.heads = heads;
+  a.seqlen_kv = 1;
+  a.stream = static_cast<cudaStream_t>(stream);
+  const cudaError_t err = launch_seqsplit_combine(a, false, x, out, lse, dtype);
+  if (err != cudaSuccess) {
+    set_error("%s: launch failed: %s", fn, cudaGetErrorString(err));
+    return MLA_ERR_CUDA;
+  }
+  return MLA_OK;
+}
+
 int32_t mla_decode_splitkv(const void* q, const void* q_pe, const void* kv, const void* k_pe,
                            void* out, float* lse, void* workspace, size_t workspace_bytes,
                            int32_t batch, int32_t heads, int32_t seqlen_kv, int32_t dtype,

@@ -148,6 +148,62 @@ struct QShape {
   int q_len, kv_heads, qb, g, hg, vb;
 };
 
+// ---------------------------------------------------------------------------
+// The sequence split's gather buffer (one per rank, the same layout everywhere;
+// mla_seqsplit_buffer_bytes):
+//   float blocks [2][world][chunk]: rank q's float32 (O, LSE) block for calls of
+//     parity p at (p * world + q) * chunk; chunk = b*h*512 O floats, then the b*h
+//     LSEs, padded to a multiple of 64 floats;
+//   a 256-byte header at round_up(2 * world * chunk * 4, 256): uint32 block flags
+//     [2][8] at byte 0, the push counter at byte 64, the status word at byte 68
+//     (0, or kErrExchange once a wait for a peer gave up);
+//   row words uint2 [2][world][rows_pad][512] after the header, then LSE words
+//     uint2 [2][world][rows_pad] (rows_pad = round_up(b*h, 64)): rank q's rows of
+//     parity p as (value bits, call number) pairs, each pair written by one 8-byte
+//     part of a 16-byte store, so a reader that sees this call's number in a pair
+//     has that pair's value (no fence or separate flag between writer and reader).
+// ---------------------------------------------------------------------------
+constexpr int kSeqMaxWorld = 8;
+constexpr uint32_t kErrExchange = 0x201;
+constexpr unsigned long long kSeqWaitNs = 2000000000ull;   // 2 s
+__host__ __device__ inline size_t seq_rows_pad(int batch, int heads) {
+  return ((size_t)batch * heads + 63) / 64 * 64;
+}
+__host__ __device__ inline size_t seq_chunk_floats(int batch, int heads) {
+  return (size_t)batch * heads * kDim + seq_rows_pad(batch, heads);
+}
+__host__ __device__ inline size_t seq_header_offset(int world, int batch, int heads) {
+  return (2 * (size_t)world * seq_chunk_floats(batch, heads) * 4 + 255) / 256 * 256;
+}
+__host__ __device__ inline size_t seq_ll_rows_offset(int world, int batch, int heads) {
+  return seq_header_offset(world, batch, heads) + 256;
+}
+__host__ __device__ inline size_t seq_ll_lse_offset(int world, int batch, int heads) {
+  return seq_ll_rows_offset(world, batch, heads) + 2 * (size_t)world * seq_rows_pad(batch, heads) * kDim * 8;
+}
+inline size_t seq_buffer_bytes(int world, int batch, int heads) {
+  return seq_ll_lse_offset(world, batch, heads) + 2 * (size_t)world * seq_rows_pad(batch, heads) * 8;
+}
+
+// Every rank's gather buffer as mapped in this process, and this call's place.
+struct PeerRows {
+  float* bufs[kSeqMaxWorld];
+  size_t chunk;     // floats per block
+  size_t header;    // byte offset of the header in a buffer
+  size_t ll_rows;   // byte offset of the row words
+  size_t ll_lse;    // byte offset of the LSE words
+  size_t rows_pad;
+  int world, rank, par;
+  uint32_t epoch;   // call number, from 1
+};
+
+// The sequence split's merge and exchange (mla_sm100.cu): `pieces` merges this
+// rank's rows from the tensor-core kernel's pieces in the workspace where it left
+// them (plan variant 1), else takes the rows this rank's block holds; the world
+// ranks' rows are then exchanged and merged into out (dtype) / lse.
+cudaError_t launch_seqsplit_combine(const DecodeArgs& a, bool pieces, const PeerRows& x, void* out, float* lse,
+                                    int dtype);
+
 // CUDA-core split-KV kernel (mla_simt.cu).  Returns a cudaError_t.
 cudaError_t launch_simt_decode(const DecodeArgs& a);
 int simt_block_n();                       // KV rows per tile of the SIMT kernel

@@ -13,13 +13,10 @@
 // every peer's call-k push, which each peer issued after its own call k - 1 merge;
 // so call k + 1 never overwrites a block a peer still reads.
 //
-// Buffer layout (every rank's is the same; mla_seqsplit_buffer_bytes):
-//   float blocks [2][world][chunk], chunk = b*h*512 + round_up(b*h, 64) floats
-//     (O of the b*h rows, then their LSEs, then padding: the packed block of the
-//     NCCL path);
-//   a 256-byte header at round_up(2*world*chunk*4, 256): uint32 flags [2][8] at
-//     byte 0 (the call number that last completed the block), the push counter at
-//     byte 64, the status word at byte 68 (0, or 0x201 when a wait gave up).
+// The buffer layout (every rank's is the same) is in mla_common.cuh; this file
+// uses its blocks, block flags, push counter and status word.  The same buffers
+// serve mla_seqsplit_decode / mla_seqsplit_merge (one launch that exchanges and
+// merges row by row, in mla_sm100.cu), which use the row flags.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <string.h>
@@ -31,9 +28,7 @@
 namespace mla {
 namespace {
 
-constexpr int kMaxWorld = 8;
-constexpr uint32_t kErrExchange = 0x201;
-constexpr unsigned long long kWaitNs = 2000000000ull;   // 2 s
+constexpr int kMaxWorld = kSeqMaxWorld;
 constexpr int kPushThreads = 256;
 constexpr int kPushBlocks = 32;
 
@@ -91,7 +86,7 @@ __global__ void __launch_bounds__(kPushThreads) mla_seqsplit_push_kernel(Xchg x)
     if (q == x.rank) continue;
     const uint32_t* f = mine + x.par * kMaxWorld + q;
     while ((int)(ld_acquire_sys(f) - x.epoch) < 0) {
-      if (now_ns() - t0 > kWaitNs) {
+      if (now_ns() - t0 > kSeqWaitNs) {
         atomicCAS(mine + 17, 0u, kErrExchange);   // a peer never delivered: the merge is invalid
         return;
       }
@@ -116,15 +111,6 @@ AddressRangeFn address_range_fn() {
   return fn;
 }
 
-size_t chunk_floats(int batch, int heads) {
-  const size_t bh = (size_t)batch * heads;
-  return bh * kDim + (bh + 63) / 64 * 64;
-}
-
-size_t header_offset(int world, int batch, int heads) {
-  return (2 * (size_t)world * chunk_floats(batch, heads) * 4 + 255) / 256 * 256;
-}
-
 }  // namespace
 }  // namespace mla
 
@@ -133,11 +119,11 @@ using namespace mla;
 extern "C" {
 
 size_t mla_seqsplit_buffer_bytes(int32_t world, int32_t batch, int32_t heads) {
-  if (world < 2 || world > kMaxWorld || batch < 1 || heads < 1) {
-    set_error("mla_seqsplit_buffer_bytes: world must be 2..%d and batch, heads >= 1", kMaxWorld);
+  if (world < 1 || world > kMaxWorld || batch < 1 || heads < 1) {
+    set_error("mla_seqsplit_buffer_bytes: world must be 1..%d and batch, heads >= 1", kMaxWorld);
     return 0;
   }
-  return header_offset(world, batch, heads) + 256;
+  return seq_buffer_bytes(world, batch, heads);
 }
 
 int32_t mla_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out) {
@@ -212,8 +198,8 @@ int32_t mla_seqsplit_exchange(void* const* bufs, int32_t world, int32_t rank, ui
     }
     x.bufs[r] = static_cast<float*>(bufs[r]);
   }
-  x.chunk = chunk_floats(batch, heads);
-  x.header = header_offset(world, batch, heads);
+  x.chunk = seq_chunk_floats(batch, heads);
+  x.header = seq_header_offset(world, batch, heads);
   x.world = world;
   x.rank = rank;
   x.par = (int)(epoch & 1u);

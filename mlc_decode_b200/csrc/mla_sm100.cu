@@ -2128,6 +2128,233 @@ mla_pair_combine_kernel(const float* __restrict__ part_lse, const float* __restr
 }
 
 // ---------------------------------------------------------------------------
+// The sequence split's merge and exchange in one launch.  Every rank holds the
+// float32 (O, LSE) of its own KV rows for every output row; the output is their
+// LSE merge over the world ranks.  CTA i takes the rows i, i + G, ... (G CTAs, at
+// most one per SM) in two passes.  Pass 1, per row: its local value (pieces mode:
+// merged from the decode kernel's pieces as the combine launch above does when
+// the sequence was split between more than fuse_max pairs; else the row the
+// decode kernel or an earlier launch wrote to this rank's block) goes to this
+// rank's block and, over NVLink, to this rank's row words in every peer's buffer:
+// each 16-byte store carries two (value bits, call number) pairs, and a reader
+// takes a pair as this call's value once it carries this call's number, so the
+// writer needs no fence and no flag (the low-latency scheme NCCL's LL protocol
+// uses).  Pass 2, per row: every thread polls its own words of each peer's row,
+// with a time limit, until they carry this call's number, then merges the world
+// rows into out / lse.  Pass 1 never waits, so no rank's stores depend on another
+// rank's progress.  Row words alternate by call parity: a rank writes call k + 1
+// only after its call k read every peer's call-k words, which each peer wrote
+// after its own call k - 1 had read the words of parity k + 1.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_pairs(uint32_t* p, float a, float b, uint32_t tag) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(__float_as_uint(a)), "r"(tag),
+               "r"(__float_as_uint(b)), "r"(tag)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_pairs(const uint32_t* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_pair(uint32_t* p, float a, uint32_t tag) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(a)), "r"(tag) : "memory");
+}
+__device__ __forceinline__ uint2 ld_pair(const uint32_t* p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+
+template <typename OutT>
+__global__ void __launch_bounds__(128 * kCombineGroups)
+mla_seqsplit_combine_kernel(const float* __restrict__ part_lse, const float* __restrict__ part_o,
+                            const uint32_t* cu, uint32_t total_fixed, int nt, int pairs, int vbatch, int heads,
+                            int hgroups, int fuse_max, const __grid_constant__ PeerRows x, OutT* __restrict__ out,
+                            float* __restrict__ lse_out) {
+  constexpr int G = kCombineGroups;
+  __shared__ float s_lse[kMaxPairs];
+  __shared__ float4 s_acc[G - 1][128];
+  const int grp = threadIdx.x >> 7, tid = threadIdx.x & 127, lane = threadIdx.x & 31;
+  const bool pieces = fuse_max >= 0;
+  ptx::grid_dep_wait();   // the decode kernel's pieces / rows are complete and visible
+  TileMap m;
+  m.cu = cu;
+  m.nt = (uint32_t)nt;
+  m.batch = vbatch;
+  m.total = !pieces ? 0u : (cu != nullptr ? __ldg(cu + vbatch) : total_fixed);
+  m.pairs = effective_pairs((uint32_t)pairs, m.total);
+  const int rows = vbatch * kHeads;
+  const size_t bh = (size_t)(vbatch / hgroups) * heads;   // output rows
+  float* own = x.bufs[x.rank] + ((size_t)x.par * x.world + x.rank) * x.chunk;
+  // rank q's row words and LSE words of this parity in buffer `buf`
+  auto row_words = [&](float* buf, int q, size_t orow) -> uint32_t* {
+    return reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(buf) + x.ll_rows) +
+           (((size_t)x.par * x.world + q) * x.rows_pad + orow) * (2 * kDim);
+  };
+  auto lse_word = [&](float* buf, int q, size_t orow) -> uint32_t* {
+    return reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(buf) + x.ll_lse) +
+           (((size_t)x.par * x.world + q) * x.rows_pad + orow) * 2;
+  };
+  // ---- pass 1: this rank's value of each row, to its block and every peer's words
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int head = r % kHeads, bb = r / kHeads;
+    const int hglob = (bb % hgroups) * kHeads + head;
+    if (hglob >= heads) continue;   // a head past h in the last head group: no row
+    const size_t orow = (size_t)(bb / hgroups) * heads + hglob;
+    int n = 0, pf = 0, pl = -1;
+    if (pieces && m.first(bb) != m.first(bb + 1)) {
+      pairs_of_sequence(m, bb, &pf, &pl);
+      n = pl - pf + 1;
+    }
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float lse = -INFINITY;
+    if (pieces && n > fuse_max) {
+      const size_t slot0 = pair_slot(m, pf, bb);
+      auto slot = [&](int k) -> size_t { return k == 0 ? slot0 : (size_t)(pf + k) * 2; };
+      const float4* po = reinterpret_cast<const float4*>(part_o) + (size_t)head * (kDim / 4) + tid;
+      constexpr size_t kSlotQuads = (size_t)kHeads * kDim / 4;
+      float4 v[kCombinePer];
+#pragma unroll
+      for (int u = 0; u < kCombinePer; ++u) {
+        const int k = grp + G * u;
+        v[u] = k < n ? __ldcg(po + slot(k) * kSlotQuads) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      for (int k = threadIdx.x; k < n; k += 128 * G) s_lse[k] = __ldcg(part_lse + slot(k) * kHeads + head);
+      __syncthreads();
+      float mx = -INFINITY;
+      for (int k = lane; k < n; k += 32) mx = fmaxf(mx, s_lse[k]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float sum = 0.f;
+      if (mx != -INFINITY)
+        for (int k = lane; k < n; k += 32) sum += exp2f((s_lse[k] - mx) * kLog2e);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      lse = mx != -INFINITY ? mx + logf(sum) : -INFINITY;
+      for (int k0 = 0;; k0 += G * kCombinePer) {
+#pragma unroll
+        for (int u = 0; u < kCombinePer; ++u) {
+          const int k = k0 + grp + G * u;
+          if (k >= n) break;
+          const float w = lse != -INFINITY ? exp2f((s_lse[k] - lse) * kLog2e) : 0.f;
+          acc.x = fmaf(w, v[u].x, acc.x);
+          acc.y = fmaf(w, v[u].y, acc.y);
+          acc.z = fmaf(w, v[u].z, acc.z);
+          acc.w = fmaf(w, v[u].w, acc.w);
+        }
+        const int k1 = k0 + G * kCombinePer;
+        if (k1 >= n) break;
+#pragma unroll
+        for (int u = 0; u < kCombinePer; ++u) {
+          const int k = k1 + grp + G * u;
+          v[u] = k < n ? __ldcg(po + slot(k) * kSlotQuads) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      if (grp > 0) s_acc[grp - 1][tid] = acc;
+      __syncthreads();
+      if (grp == 0) {
+#pragma unroll
+        for (int g2 = 0; g2 < G - 1; ++g2) {
+          const float4 o = s_acc[g2][tid];
+          acc.x += o.x;
+          acc.y += o.y;
+          acc.z += o.z;
+          acc.w += o.w;
+        }
+        reinterpret_cast<float4*>(own + orow * kDim)[tid] = acc;
+        if (tid == 0) own[bh * kDim + orow] = lse;
+      }
+    } else if (grp == 0) {
+      acc = __ldcg(reinterpret_cast<const float4*>(own + orow * kDim) + tid);
+      lse = __ldcg(own + bh * kDim + orow);
+    }
+    if (grp == 0) {
+      for (int q = 0; q < x.world; ++q) {
+        if (q == x.rank) continue;
+        uint32_t* w = row_words(x.bufs[q], x.rank, orow) + 8 * tid;
+        st_pairs(w, acc.x, acc.y, x.epoch);
+        st_pairs(w + 4, acc.z, acc.w, x.epoch);
+        if (tid == 0) st_pair(lse_word(x.bufs[q], x.rank, orow), lse, x.epoch);
+      }
+    }
+    __syncthreads();   // s_lse and s_acc are free for the next row
+  }
+  // ---- pass 2: every peer's value of each row (polled), then the merge
+  if (grp != 0) return;
+  uint32_t* status = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(x.bufs[x.rank]) + x.header) + 17;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int head = r % kHeads, bb = r / kHeads;
+    const int hglob = (bb % hgroups) * kHeads + head;
+    if (hglob >= heads) continue;
+    const size_t orow = (size_t)(bb / hgroups) * heads + hglob;
+    float lq[kSeqMaxWorld];
+    float4 vq[kSeqMaxWorld];
+    bool ok = true;
+#pragma unroll
+    for (int q = 0; q < kSeqMaxWorld; ++q) {
+      lq[q] = -INFINITY;
+      vq[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (q >= x.world || !ok) continue;
+      if (q == x.rank) {
+        vq[q] = __ldcg(reinterpret_cast<const float4*>(own + orow * kDim) + tid);
+        lq[q] = __ldcg(own + bh * kDim + orow);
+        continue;
+      }
+      const uint32_t* w = row_words(x.bufs[x.rank], q, orow) + 8 * tid;
+      const uint32_t* lw = lse_word(x.bufs[x.rank], q, orow);
+      uint4 a = ld_pairs(w), b2 = ld_pairs(w + 4);
+      uint2 l2 = ld_pair(lw);
+      if (a.y != x.epoch || a.w != x.epoch || b2.y != x.epoch || b2.w != x.epoch || l2.y != x.epoch) {
+        const uint64_t t0 = ptx::globaltimer();
+        for (;;) {
+          a = ld_pairs(w);
+          b2 = ld_pairs(w + 4);
+          l2 = ld_pair(lw);
+          if (a.y == x.epoch && a.w == x.epoch && b2.y == x.epoch && b2.w == x.epoch && l2.y == x.epoch) break;
+          // give up at the time limit, or at once when another thread already has
+          if (*reinterpret_cast<volatile uint32_t*>(status) != 0u || ptx::globaltimer() - t0 > kSeqWaitNs) {
+            atomicCAS(status, 0u, kErrExchange);   // a peer never delivered: the merge is invalid
+            ok = false;
+            break;
+          }
+          __nanosleep(32);
+        }
+      }
+      vq[q] = make_float4(__uint_as_float(a.x), __uint_as_float(a.z), __uint_as_float(b2.x), __uint_as_float(b2.z));
+      lq[q] = __uint_as_float(l2.x);
+    }
+    if (!ok) return;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kSeqMaxWorld; ++q) mx = fmaxf(mx, lq[q]);
+    float sum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (mx != -INFINITY) {
+#pragma unroll
+      for (int q = 0; q < kSeqMaxWorld; ++q) {
+        const float w = exp2f((lq[q] - mx) * kLog2e);   // 0 for the unused slots (lq = -inf)
+        sum += w;
+        acc.x = fmaf(w, vq[q].x, acc.x);
+        acc.y = fmaf(w, vq[q].y, acc.y);
+        acc.z = fmaf(w, vq[q].z, acc.z);
+        acc.w = fmaf(w, vq[q].w, acc.w);
+      }
+      const float inv = 1.f / sum;
+      acc.x *= inv;
+      acc.y *= inv;
+      acc.z *= inv;
+      acc.w *= inv;
+    }
+    const float lse = mx != -INFINITY ? mx + logf(sum) : -INFINITY;
+    store4_out(out + orow * kDim + 4 * tid, acc);
+    if (lse_out != nullptr && tid == 0) lse_out[orow] = lse;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Plan of a ragged call (per-sequence KV lengths), one CTA: cu[v] = first tile of
 // virtual sequence v (qb x head groups + 1 entries, qb query sequences of `heads`
 // rows) over the lengths qseq_len gives (seqlens nullptr: max_len for all); query
@@ -2605,6 +2832,48 @@ cudaError_t launch_sm100_combine(const DecodeArgs& a) {
                               static_cast<__nv_bfloat16*>(a.out), a.lse, cu, total, nt, pairs, vb, g, hg, fm);
   return cudaLaunchKernelEx(&cfg, mla_pair_combine_kernel<__half>, pl, po, static_cast<__half*>(a.out), a.lse, cu,
                             total, nt, pairs, vb, g, hg, fm);
+}
+
+cudaError_t launch_seqsplit_combine(const DecodeArgs& a, bool pieces, const PeerRows& x, void* out, float* lse,
+                                    int dtype) {
+  using namespace sm100;
+  const int nt = (a.seqlen_kv + kTile - 1) / kTile;
+  const QShape qs = qshape(a);
+  const int hg = qs.hg, vb = qs.vb;
+  const uint32_t total = (uint32_t)vb * (uint32_t)nt;
+  // at most one CTA per SM: pass 1 of every CTA runs without waiting on anything
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (sms[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    sms[dev] = n > 0 ? n : 1;
+  }
+  const int rows = vb * kHeads;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(rows < sms[dev] ? rows : sms[dev], 1, 1);
+  cfg.blockDim = dim3(128 * kCombineGroups, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const float* pl = a.part_lse;
+  const float* po = a.part_o;
+  const uint32_t* cu = a.cu_tiles;
+  const int pairs = a.plan.bpc, g = qs.g, fm = pieces ? kFuseMaxPieces : -1;
+  if (dtype == MLA_DTYPE_BF16)
+    return cudaLaunchKernelEx(&cfg, mla_seqsplit_combine_kernel<__nv_bfloat16>, pl, po, cu, total, nt, pairs, vb, g, hg,
+                              fm, x, static_cast<__nv_bfloat16*>(out), lse);
+  if (dtype == MLA_DTYPE_F16)
+    return cudaLaunchKernelEx(&cfg, mla_seqsplit_combine_kernel<__half>, pl, po, cu, total, nt, pairs, vb, g, hg, fm,
+                              x, static_cast<__half*>(out), lse);
+  return cudaLaunchKernelEx(&cfg, mla_seqsplit_combine_kernel<float>, pl, po, cu, total, nt, pairs, vb, g, hg, fm, x,
+                            static_cast<float*>(out), lse);
 }
 
 }  // namespace mla

@@ -189,6 +189,35 @@ class MlaDecodeKernel:
                             lse.data_ptr(), ws.data_ptr(), ws.numel(), b, h, s, _DTYPES[dtype],
                             self._ccfg, stream)
 
+    def seqsplit(self, q, q_pe, kv, k_pe, out, lse, bufs, world: int, rank: int, epoch: int):
+        """This KV part of a sequence split across ranks, and the exchange and merge
+        with the other ranks' parts in one more launch (mla_seqsplit_decode): ``out``
+        ([batch, heads, 512], q's dtype) and ``lse`` (float32 or None) receive the
+        decode over every rank's rows.  ``bufs``: every rank's gather buffer (device
+        pointers, a ctypes c_void_p array or a sequence); ``epoch``: this call's
+        number, from 1, the same on every rank.  Every rank must call it.
+        """
+        self._one_kv_head("seqsplit")
+        b, h, s = self.batch, self.heads, self.seqlen_kv
+        dtype = q.dtype if isinstance(q, torch.Tensor) else None
+        if dtype not in _DTYPES:
+            raise ValueError(f"q must be float16 or bfloat16, got {dtype}")
+        dev = q.device
+        shapes = self._shapes
+        checks = [("q", q, shapes[0], dtype), ("q_pe", q_pe, shapes[1], dtype), ("kv", kv, shapes[2], dtype),
+                  ("k_pe", k_pe, shapes[3], dtype), ("out", out, shapes[0], dtype)]
+        if lse is not None:
+            checks.append(("lse", lse, shapes[0][:2], torch.float32))
+        for name, t, shape, dt in checks:
+            if not (type(t) is torch.Tensor and t.dtype == dt and t.device == dev and t.shape == shape
+                    and t.is_contiguous() and dev.type == "cuda"):
+                _check_tensor(name, t, shape, dt, dev)
+        ws = self._workspace(dev, dtype)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        capi.seqsplit_decode(q.data_ptr(), q_pe.data_ptr(), kv.data_ptr(), k_pe.data_ptr(), out.data_ptr(),
+                             None if lse is None else lse.data_ptr(), ws.data_ptr(), ws.numel(), b, h, s,
+                             _DTYPES[dtype], bufs, world, rank, epoch, self._ccfg, stream)
+
     def splitkv(self, q, q_pe, kv, k_pe, out, lse=None):
         """First launch of a call only (the split-KV kernel); pair with ``combine_ws``.
 

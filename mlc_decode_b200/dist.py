@@ -73,10 +73,15 @@ class SequenceSplitDecoder:
 
     ``partial_fn(q, q_pe, kv, k_pe, o, lse)`` and ``combine_fn(part_lse,
     part_o, out, lse)`` default to the CUDA kernels; tests on CPU ranks pass
-    their own.  Every rank's (O, LSE) lives in one packed block of a
-    [world, b*h*513 + padding] float32 buffer, so a call issues a single
-    all-gather (in place) and the merge reads the gathered blocks where they
-    landed (``combine`` with a split stride).
+    their own.  Exchange over NVLink peer memory (``exchange`` "p2p", or "auto"
+    with every rank on one node with peer access and an NCCL group): a call is
+    two launches, this rank's decode and one launch that merges its rows,
+    stores each into every peer's gather buffer with a per-row flag and merges
+    the peers' rows as they arrive (``MlaDecodeKernel.seqsplit``).  Otherwise
+    every rank's (O, LSE) lives in one packed block of a [world, b*h*513 +
+    padding] float32 buffer, a call issues a single all-gather (in place) and
+    the merge reads the gathered blocks where they landed (``combine`` with a
+    split stride).  Every rank passes ``out`` of the same dtype.
     """
 
     def __init__(self, batch: int, heads: int, seqlen_kv: int, group=None, cfg=None,
@@ -179,7 +184,7 @@ class SequenceSplitDecoder:
         if not self._p2p:
             return 0
         buf = self._p2p[0]
-        hdr = buf.numel() - 256
+        hdr = -(-2 * self.world * self._chunk() * 4 // 256) * 256   # the header follows the blocks
         return int(buf[hdr + 68: hdr + 72].view(torch.int32).item())
 
     def close(self):
@@ -204,8 +209,21 @@ class SequenceSplitDecoder:
 
     # -- the call ---------------------------------------------------------------
     def __call__(self, q, q_pe, kv_part, k_pe_part, out, lse=None):
+        dev = q.device
+        if (self.kernel is not None and self._partial == self.kernel.partial and self._combine is combine
+                and isinstance(q, torch.Tensor) and out.dtype == q.dtype and self._use_p2p(dev)
+                and self._out_ok(out, lse, dev)):
+            # over NVLink peer memory: this rank's decode, then one launch that merges
+            # its rows, stores them into every peer's buffer and merges theirs
+            if kv_part.shape[1] != self.local_len or k_pe_part.shape[1] != self.local_len:
+                raise ValueError(f"rank {self.rank} holds KV rows [{self.start}, {self.end}): "
+                                 f"expected {self.local_len} rows, got {kv_part.shape[1]}")
+            self._epoch += 1
+            self.kernel.seqsplit(q, q_pe, kv_part, k_pe_part, out, lse, self._p2p[4], self.world, self.rank,
+                                 self._epoch)
+            return
         self.local(q, q_pe, kv_part, k_pe_part)
-        self.merge(out, lse, q.device)
+        self.merge(out, lse, dev)
 
     def local(self, q, q_pe, kv_part, k_pe_part):
         """This rank's part: normalised float32 O and LSE of its KV rows, written
@@ -238,16 +256,16 @@ class SequenceSplitDecoder:
         if self._use_p2p(dev):
             from . import capi
 
-            par = self._epoch & 1
-            _, _, o_all, l_all, o_ptr, l_ptr = self._p2p_views(par)
             stream = torch.cuda.current_stream(dev).cuda_stream
-            capi.seqsplit_exchange_raw(self._p2p[4], w, self.rank, self._epoch, b, h, stream)
             if self._combine is combine and self._out_ok(out, lse, dev):
-                # the blocks' layout was checked when the views were made
-                capi.combine_strided(l_ptr, self._chunk(), o_ptr, self._chunk(), w, b, h, out.data_ptr(),
-                                     None if lse is None else lse.data_ptr(), _OUT_TYPES[out.dtype], stream)
-            else:
-                self._combine(l_all, o_all, out, lse)
+                # one launch: this rank's rows into every peer's buffer, row flags, the merge
+                capi.seqsplit_merge(self._p2p[4], w, self.rank, self._epoch, b, h, out.data_ptr(),
+                                    None if lse is None else lse.data_ptr(), _OUT_TYPES[out.dtype], stream)
+                return
+            # a caller's combine_fn: the block exchange, then that merge
+            _, _, o_all, l_all, _, _ = self._p2p_views(self._epoch & 1)
+            capi.seqsplit_exchange_raw(self._p2p[4], w, self.rank, self._epoch, b, h, stream)
+            self._combine(l_all, o_all, out, lse)
             return
         buf, _, _ = self._buffers(dev)
         dist.all_gather_into_tensor(buf.view(-1), buf[self.rank], group=self.group)

@@ -2,8 +2,9 @@
 
 Checks, on every rank, (a) the batch split (this rank's block of sequences,
 no collective) and (b) the sequence split (this rank's part of every KV
-cache, float32 partials all-gathered and merged), both against the float64
-oracle.  Exits non-zero on a parity failure.
+cache; float32 partials exchanged over NVLink peer memory or all-gathered,
+then merged), both against the float64 oracle.  Exits non-zero on a parity
+failure.
 """
 import datetime
 import os
@@ -41,24 +42,41 @@ def main():
         print(f"rank {rank} batch split {res}", flush=True)
         ok &= res["ok"]
         # (b) sequence split, both exchanges (over NVLink peer memory, and the NCCL
-        # all-gather), each called three times (both halves of the double buffer)
-        b, h, s = 2, 128, 20000
-        inputs = O.make_inputs(b, h, s, "bf16", seed=72)
-        ref, rl = O.ref_program_f64(*inputs)
-        for exchange in ("p2p", "collective"):
+        # all-gather), each called three times (both halves of the double buffer).
+        # p2p: the one-call path (decode, then one launch that merges this rank's
+        # pieces, pushes its rows and merges the peers'), then two calls through the
+        # halves (local() into the block, merge() = exchange and merge of the blocks'
+        # rows), then one through a caller's combine (the block exchange kernel).
+        from mlc_decode_b200 import combine
+
+        cases = [(2, 128, 20000, "bf16", "p2p"), (2, 128, 20000, "bf16", "collective"),
+                 (3, 64, 9000, "fp16", "p2p")]
+        for b, h, s, dt, exchange in cases:
+            inputs = O.make_inputs(b, h, s, dt, seed=72 + h)
+            ref, rl = O.ref_program_f64(*inputs)
             dec = SequenceSplitDecoder(b, h, s, exchange=exchange)
             q, qp = inputs[0].to(dev), inputs[1].to(dev)
             kv = inputs[2][:, dec.start:dec.end].contiguous().to(dev)
             kp = inputs[3][:, dec.start:dec.end].contiguous().to(dev)
-            for call in range(3):
-                out = torch.full((b, h, 512), float("nan"), dtype=torch.bfloat16, device=dev)
+            routes = ["call"] * 3 if exchange == "collective" or h != 128 else ["call", "call", "halves", "halves",
+                                                                                 "call", "combine_fn"]
+            for call, route in enumerate(routes):
+                out = torch.full((b, h, 512), float("nan"), dtype=q.dtype, device=dev)
                 lse = torch.full((b, h), float("nan"), device=dev)
-                dec(q, qp, kv, kp, out, lse)
+                if route == "call":
+                    dec(q, qp, kv, kp, out, lse)
+                elif route == "halves":
+                    dec.local(q, qp, kv, kp)
+                    dec.merge(out, lse)
+                else:
+                    dec._combine = lambda l_all, o_all, o, l: combine(l_all, o_all, o, l)
+                    dec(q, qp, kv, kp, out, lse)
+                    dec._combine = combine
                 torch.cuda.synchronize()
-                res = O.check_parity(out.float().cpu().numpy(), lse.cpu().numpy(), ref, rl, "bf16")
+                res = O.check_parity(out.float().cpu().numpy(), lse.cpu().numpy(), ref, rl, dt)
                 res["exchange_status"] = dec.exchange_status()
-                print(f"rank {rank} sequence split ({exchange}, call {call}) rows [{dec.start}, {dec.end}) {res}",
-                      flush=True)
+                print(f"rank {rank} sequence split b{b} h{h} {dt} ({exchange}, call {call}, {route}) "
+                      f"rows [{dec.start}, {dec.end}) {res}", flush=True)
                 ok &= res["ok"] and res["exchange_status"] == 0
             dist.barrier()
             dec.close()

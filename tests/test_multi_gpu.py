@@ -32,5 +32,6 @@ def test_two_gpu_batch_and_sequence_split():
            os.path.join(HERE, "mgpu_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    # per rank: the batch split, then 3 calls of each sequence-split exchange
-    assert r.stdout.count("'ok': True") == 2 * (1 + 2 * 3), r.stdout
+    # per rank: the batch split, then the sequence-split calls of mgpu_worker's cases
+    # (6 over peer memory at b2 h128, 3 over the all-gather, 3 over peer memory at b3 h64)
+    assert r.stdout.count("'ok': True") == 2 * (1 + 6 + 3 + 3), r.stdout
