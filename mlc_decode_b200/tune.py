@@ -60,7 +60,9 @@ def candidates(batch, heads, seqlen_kv):
     return out
 
 
-def time_shape(batch, heads, seqlen_kv, dtype_name, reps=8, calls=10):
+def time_shape(batch, heads, seqlen_kv, dtype_name, reps=8, calls=10, cands=None):
+    """Median device time per call of each candidate config (default: ``candidates``)
+    on seeded inputs of one shape: (candidates, medians in us, index of the fastest)."""
     dt = DT[dtype_name]
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
@@ -69,7 +71,7 @@ def time_shape(batch, heads, seqlen_kv, dtype_name, reps=8, calls=10):
     kv = torch.randn(batch, seqlen_kv, 1, 512, device=dev, generator=g).to(dt)
     kp = torch.randn(batch, seqlen_kv, 1, 64, device=dev, generator=g).to(dt)
     out = torch.empty_like(q)
-    cands = candidates(batch, heads, seqlen_kv)
+    cands = candidates(batch, heads, seqlen_kv) if cands is None else list(cands)
     kerns = [MlaDecodeKernel(batch, heads, 1, seqlen_kv, cfg=c) for c in cands]
     for k in kerns:
         for _ in range(3):
