@@ -137,3 +137,40 @@ def test_kernel_object_rejects_non_absorbed_shapes():
     k = MlaDecodeKernel(1, 16, 2, 64, 512, 64)   # grouped KV heads: the mla_decode_ext path
     with pytest.raises(NotImplementedError):
         k.plan()
+
+
+def test_seqsplit_buffer_layout_sizes(lib):
+    """mla_seqsplit_buffer_bytes: float32 (O, LSE) blocks [2][world][chunk], a 256-byte
+    header, then (value, call number) words for rows and LSEs; world 1..8."""
+    for world in range(1, 9):
+        for b, h in ((1, 128), (3, 64), (2, 16), (5, 200)):
+            bh = b * h
+            rows_pad = -(-bh // 64) * 64
+            chunk = bh * 512 + rows_pad
+            header = -(-2 * world * chunk * 4 // 256) * 256
+            ll_lse = header + 256 + 2 * world * rows_pad * 512 * 8
+            assert capi.seqsplit_buffer_bytes(world, b, h) == ll_lse + 2 * world * rows_pad * 8
+    for bad in ((0, 1, 128), (9, 1, 128), (2, 0, 128), (2, 1, 0)):
+        assert lib.mla_seqsplit_buffer_bytes(*bad) == 0
+
+
+def test_seqsplit_entry_points_reject_bad_arguments_without_touching_the_gpu(lib):
+    cfg = capi.make_cfg({})
+    arr = (ctypes.c_void_p * 2)(256, 512)
+    dec = lib.mla_seqsplit_decode
+    # world out of range, rank outside the world, call number 0, no buffers
+    for world, rank, epoch, bufs in ((0, 0, 1, arr), (9, 0, 1, arr), (2, 2, 1, arr), (2, 0, 0, arr), (2, 0, 1, None)):
+        rc = dec(256, 256, 256, 256, 256, None, 256, 1 << 20, 1, 128, 1024, 1, bufs, world, rank, epoch,
+                 ctypes.byref(cfg), None)
+        assert rc == 1 and "bad argument" in capi.last_error(), (world, rank, epoch)
+    # a buffer that is not 256-byte aligned
+    odd = (ctypes.c_void_p * 2)(256, 528)
+    rc = dec(256, 256, 256, 256, 256, None, 256, 1 << 20, 1, 128, 1024, 1, odd, 2, 0, 1, ctypes.byref(cfg), None)
+    assert rc == 1 and "256-byte" in capi.last_error()
+    # a null or misaligned output
+    rc = dec(256, 256, 256, 256, None, None, 256, 1 << 20, 1, 128, 1024, 1, arr, 2, 0, 1, ctypes.byref(cfg), None)
+    assert rc == 1 and "out" in capi.last_error()
+    mrg = lib.mla_seqsplit_merge
+    assert mrg(arr, 2, 0, 1, 1, 128, 264, None, 1, None) == 1 and "aligned" in capi.last_error()
+    assert mrg(arr, 2, 0, 1, 1, 128, 256, None, 7, None) == 1 and "dtype" in capi.last_error()
+    assert mrg(arr, 2, 5, 1, 1, 128, 256, None, 1, None) == 1 and "bad argument" in capi.last_error()
