@@ -29,8 +29,9 @@ def main():
     try:
         dev = torch.device("cuda", local)
         # (a) batch split
-        inputs = O.make_inputs(6, 128, 1000, "bf16", seed=71)
-        sl = batch_shard(6, rank, world)
+        nb = max(6, world)   # every rank gets at least one sequence
+        inputs = O.make_inputs(nb, 128, 1000, "bf16", seed=71)
+        sl = batch_shard(nb, rank, world)
         mine = [t[sl].contiguous() for t in inputs]
         q, qp, kv, kp = (t.to(dev) for t in mine)
         out = torch.empty_like(q)

@@ -82,7 +82,8 @@ def _ref(inputs):
 
 
 @pytest.mark.parametrize("cfg", [None, {"kernel": "simt", "num_split": 3}], ids=["auto", "simt"])
-@pytest.mark.parametrize("b,h,s,dt", [(1, 128, 20000, "bf16"), (2, 128, 3000, "fp16"), (3, 64, 5000, "bf16")])
+@pytest.mark.parametrize("b,h,s,dt", [(1, 128, 20000, "bf16"), (2, 128, 3000, "fp16"), (3, 64, 5000, "bf16"),
+                                     (1, 256, 9000, "bf16")])
 def test_world1_matches_whole_decode(b, h, s, dt, cfg, cuda):
     """auto: one sequence split between many CTA pairs, merged from its pieces in the
     exchange launch (b1), or rows the decode kernel wrote whole; simt: the CUDA-core
@@ -104,7 +105,7 @@ def test_world1_matches_whole_decode(b, h, s, dt, cfg, cuda):
         assert _status(buf, 1, b, h) == 0
 
 
-@pytest.mark.parametrize("b,h,s,dt", [(1, 128, 40000, "bf16"), (3, 64, 9000, "fp16")])
+@pytest.mark.parametrize("b,h,s,dt", [(1, 128, 40000, "bf16"), (3, 64, 9000, "fp16"), (2, 256, 6000, "bf16")])
 def test_world2_emulated_peer(b, h, s, dt, cuda):
     """Rank 0's launch against a peer whose rows and flags are already in place."""
     from mlc_decode_b200 import MlaDecodeKernel
